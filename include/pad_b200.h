@@ -1,0 +1,121 @@
+/*
+ * pad_b200.h -- C ABI of the B200 (sm_100a) paged-attention decode library
+ * (libpad_b200.so).
+ *
+ * Every entry point takes plain pointers, sizes and strides (in ELEMENTS),
+ * never framework types, and returns a pad_status code. Pointers to tensors
+ * are device pointers on the device that is current when the call is made.
+ * Calls are asynchronous on the given CUDA stream (a cudaStream_t passed as
+ * void*; NULL means the legacy default stream) and never synchronise the
+ * device.
+ *
+ * The decode entry point replaces, as one C call, the reference project's
+ * pybind binding ``forward_v4(q, k_cache, v_cache, block_table, seq_lens,
+ * scale, gqa_ratio, head_dim, page_size, num_splits)`` (cuda/binding.cpp:13-14,
+ * declared at cuda/kernels.h:60-70) and the launcher behind it
+ * (cuda/kernel_v4_split_k.cu:205-268). Differences, by design:
+ *   - the caller owns `out` and a reusable `workspace` (the reference
+ *     allocated both with torch on every call, cuda/kernel_v4_split_k.cu:228-232);
+ *   - the stream is explicit (the reference launched on the legacy default
+ *     stream, cuda/kernel_v4_split_k.cu:238,257);
+ *   - argument errors come back as status codes instead of TORCH_CHECK
+ *     exceptions (cuda/kernel_v4_split_k.cu:216-223).
+ *
+ * Tensor layouts (the reference's, README.md:38-44):
+ *   q, out       [batch, num_q_heads, head_dim]            fp16
+ *   k/v_cache    [num_pages, page_size, num_kv_heads, head_dim] fp16
+ *   block_table  [batch, max_pages_per_seq]                int32
+ *   seq_lens     [batch]                                   int32
+ * The last dimension of q, out, k_cache and v_cache must be contiguous
+ * (stride 1); the other strides of q/k_cache/v_cache must be multiples of
+ * 8 elements (16 bytes, a TMA requirement) and the base pointers 16-byte
+ * aligned. block_table's inner stride must be 1.
+ */
+#ifndef PAD_B200_H_
+#define PAD_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum pad_status {
+  PAD_OK = 0,
+  PAD_ERR_INVALID_ARGUMENT = 1, /* a shape, size or pointer is invalid      */
+  PAD_ERR_UNSUPPORTED = 2,      /* valid but outside what the kernels cover */
+  PAD_ERR_WORKSPACE = 3,        /* workspace missing or too small           */
+  PAD_ERR_CUDA = 4,             /* a CUDA runtime/driver call failed        */
+} pad_status;
+
+/* Bits OR-ed into *error_flags by the kernels (value checks the reference's
+ * oracle performs on the host, src/reference.py:40-41,107-112, done here on
+ * the device without a host sync). */
+#define PAD_FLAG_BAD_PAGE_ID 0x1     /* a block_table entry outside [0, num_pages) */
+#define PAD_FLAG_SEQ_LEN_RANGE 0x2   /* seq_len < 0 or > max_pages_per_seq * page_size */
+#define PAD_FLAG_WAIT_TIMEOUT 0x100  /* an in-kernel wait gave up (never expected) */
+
+/* Human-readable text for a status code (static storage). */
+const char* pad_status_string(int status);
+
+/* Text of the last error on the calling thread (static thread-local storage). */
+const char* pad_last_error(void);
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int pad_version(void);
+
+/* Number of SMs of `device` and how many decode CTAs one SM holds for the
+ * given head_dim / gqa_ratio (the inputs of the split heuristic). */
+int pad_device_info(int device, int64_t head_dim, int64_t gqa_ratio, int* num_sms, int* ctas_per_sm);
+
+/* Number of persistent decode CTAs (work partitions) the decode call will
+ * launch for this problem on `device`.
+ *   num_splits <= 0 : heuristic -- one partition per resident CTA slot
+ *                     (num_sms * ctas_per_sm), capped by the number of
+ *                     64-token tiles the batch can hold;
+ *   num_splits >= 1 : num_splits partitions per (sequence, KV head) pair,
+ *                     i.e. num_splits * batch * num_kv_heads partitions. */
+int pad_decode_partitions(int device, int64_t batch, int64_t num_kv_heads, int64_t gqa_ratio,
+                          int64_t head_dim, int64_t page_size, int64_t max_pages_per_seq,
+                          int64_t num_splits, int64_t* partitions);
+
+/* Bytes of device workspace pad_paged_attention_decode needs for this
+ * problem (same arguments as pad_decode_partitions). The workspace holds the
+ * fp32 split partials (O, m, l) and per-partition merge descriptors; it
+ * needs no initialisation and may be reused by consecutive calls on one
+ * stream (calls that overlap in time must use distinct workspaces). */
+int pad_decode_workspace_bytes(int device, int64_t batch, int64_t num_kv_heads, int64_t gqa_ratio,
+                               int64_t head_dim, int64_t page_size, int64_t max_pages_per_seq,
+                               int64_t num_splits, size_t* bytes);
+
+/* Decode attention over a paged fp16 KV cache with GQA.
+ *
+ *   out[b, h, :] = softmax(scale * q[b, h, :] . K_b[h / G]^T) @ V_b[h / G]
+ *
+ * where K_b/V_b are the first seq_lens[b] token rows of the pages
+ * block_table[b, 0 .. ceil(seq_lens[b] / page_size) - 1] and
+ * G = num_q_heads / num_kv_heads. A sequence with seq_len == 0 yields a zero
+ * row (src/reference.py:32-34). Entries of block_table past a sequence's
+ * last page are never read.
+ *
+ * Strides are in elements: q_strides[3], k_strides[4], v_strides[4],
+ * out_strides[3]; block_table_stride is the row stride of block_table.
+ * error_flags (device int32, optional) receives PAD_FLAG_* bits; it is
+ * OR-ed into, never cleared.
+ */
+int pad_paged_attention_decode(const void* q, const void* k_cache, const void* v_cache,
+                               const int32_t* block_table, const int32_t* seq_lens, void* out,
+                               int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
+                               int64_t head_dim, int64_t num_pages, int64_t page_size,
+                               int64_t max_pages_per_seq, const int64_t* q_strides,
+                               const int64_t* k_strides, const int64_t* v_strides,
+                               int64_t block_table_stride, const int64_t* out_strides, float scale,
+                               int64_t num_splits, void* workspace, size_t workspace_bytes,
+                               void* stream, int32_t* error_flags);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PAD_B200_H_ */

@@ -1,0 +1,386 @@
+// pad_decode.cu -- host side of libpad_b200.so: argument checks, TMA tensor
+// map encoding, kernel-instance dispatch and the extern "C" entry points
+// declared in include/pad_b200.h.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "pad_b200.h"
+#include "pad_decode_kernels.cuh"
+
+namespace {
+
+using namespace pad;
+
+thread_local std::string g_last_error;
+
+int fail(int status, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(PAD_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// ----------------------------------------------------------------- instances
+struct Instance {
+  const void* kernel;          // decode_stream_kernel<TR>
+  const void* merge;           // merge_kernel<D>
+  int smem_bytes;
+  int qrows;
+  int segw;                    // bytes per row segment (TMA box inner extent)
+  bool swz;
+};
+
+template <int D>
+constexpr int stages_for() {
+  return D >= 128 ? 3 : (D == 64 ? 6 : 8);
+}
+
+template <int D, int NT, bool SWZ>
+Instance make_instance() {
+  using TR = Traits<D, NT, SWZ, stages_for<D>()>;
+  Instance in;
+  in.kernel = reinterpret_cast<const void*>(&decode_stream_kernel<TR>);
+  in.merge = reinterpret_cast<const void*>(&merge_kernel<D>);
+  in.smem_bytes = TR::SMEM_BYTES;
+  in.qrows = TR::QROWS;
+  in.segw = TR::SEGW;
+  in.swz = SWZ;
+  return in;
+}
+
+template <int D>
+bool pick_nt_swz(int nt, bool swz, Instance* out) {
+  if (nt == 1) *out = swz ? make_instance<D, 1, true>() : make_instance<D, 1, false>();
+  else *out = swz ? make_instance<D, 2, true>() : make_instance<D, 2, false>();
+  return true;
+}
+
+bool pick_instance(int64_t head_dim, int64_t gqa, bool swz, Instance* out) {
+  const int nt = gqa <= 8 ? 1 : 2;
+  switch (head_dim) {
+    case 16: return pick_nt_swz<16>(nt, swz, out);
+    case 32: return pick_nt_swz<32>(nt, swz, out);
+    case 64: return pick_nt_swz<64>(nt, swz, out);
+    case 128: return pick_nt_swz<128>(nt, swz, out);
+    default: return false;
+  }
+}
+
+// Largest power of two that divides page_size, capped at one tile: the rows
+// of one TMA box. Boxes never straddle a page or a tile.
+int box_rows_for(int64_t page_size) {
+  int r = 1;
+  while (r < kTile && page_size % (2 * r) == 0) r *= 2;
+  return r;
+}
+
+// Per-device, per-instance cached facts: opt-in shared memory set, occupancy.
+constexpr int kMaxDevices = 64;
+constexpr int kNumInstanceKeys = 4 * 2 * 2;
+struct DeviceCache {
+  int num_sms = 0;
+  int occ[kNumInstanceKeys] = {};
+  bool smem_set[kNumInstanceKeys] = {};
+};
+DeviceCache g_dev[kMaxDevices];
+std::mutex g_mu;
+
+int instance_key(int64_t head_dim, int64_t gqa, bool swz) {
+  const int di = head_dim == 16 ? 0 : head_dim == 32 ? 1 : head_dim == 64 ? 2 : 3;
+  return (di * 2 + (gqa <= 8 ? 0 : 1)) * 2 + (swz ? 1 : 0);
+}
+
+int prepare_device(int device, const Instance& in, int key, int* num_sms, int* occ) {
+  if (device < 0 || device >= kMaxDevices) return fail(PAD_ERR_INVALID_ARGUMENT, "device %d out of range", device);
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceCache& dc = g_dev[device];
+  if (dc.num_sms == 0) {
+    int n = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+    dc.num_sms = n;
+  }
+  if (!dc.smem_set[key]) {
+    int cur = -1;
+    cudaError_t e = cudaGetDevice(&cur);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (cur != device && (e = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    e = cudaFuncSetAttribute(in.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, in.smem_bytes);
+    int o = 0;
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, in.kernel, kThreads, in.smem_bytes);
+    if (cur != device) cudaSetDevice(cur);
+    if (e != cudaSuccess) return cuda_fail(e, "configuring the decode kernel");
+    if (o < 1) return fail(PAD_ERR_UNSUPPORTED, "decode kernel does not fit on an SM (%d B smem)", in.smem_bytes);
+    dc.occ[key] = o;
+    dc.smem_set[key] = true;
+  }
+  *num_sms = dc.num_sms;
+  *occ = dc.occ[key];
+  return PAD_OK;
+}
+
+// ----------------------------------------------------------------- planning
+struct Plan {
+  Instance inst;
+  int key = 0;
+  int box_rows = 1;
+  int64_t partitions = 0;
+  int64_t slots = 0;
+  size_t off_meta = 0, off_ml = 0, off_o = 0, bytes = 0;
+};
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+int make_plan(int device, int64_t batch, int64_t hkv, int64_t gqa, int64_t head_dim, int64_t page_size,
+              int64_t max_pages, int64_t num_splits, Plan* plan) {
+  if (batch < 0 || hkv <= 0 || gqa <= 0 || page_size <= 0 || max_pages < 0)
+    return fail(PAD_ERR_INVALID_ARGUMENT,
+                "invalid sizes: batch=%lld num_kv_heads=%lld gqa_ratio=%lld page_size=%lld max_pages=%lld",
+                (long long)batch, (long long)hkv, (long long)gqa, (long long)page_size, (long long)max_pages);
+  if (head_dim != 16 && head_dim != 32 && head_dim != 64 && head_dim != 128)
+    return fail(PAD_ERR_UNSUPPORTED, "head_dim %lld not supported (16, 32, 64 or 128)", (long long)head_dim);
+  if (gqa > 16) return fail(PAD_ERR_UNSUPPORTED, "gqa_ratio %lld > 16 not supported", (long long)gqa);
+  const int64_t cap = max_pages * page_size;
+  const int64_t tiles_max = (cap + kTile - 1) / kTile;
+  const int64_t tiles_ub = batch * hkv * tiles_max;
+  if (cap > INT32_MAX || tiles_ub > INT32_MAX / 2)
+    return fail(PAD_ERR_UNSUPPORTED, "problem too large for 32-bit tile indexing (%lld tiles)", (long long)tiles_ub);
+  plan->box_rows = box_rows_for(page_size);
+  const bool swz = plan->box_rows >= 8;
+  if (!pick_instance(head_dim, gqa, swz, &plan->inst))
+    return fail(PAD_ERR_UNSUPPORTED, "no kernel instance for head_dim %lld", (long long)head_dim);
+  plan->key = instance_key(head_dim, gqa, swz);
+  int sms = 0, occ = 0;
+  int st = prepare_device(device, plan->inst, plan->key, &sms, &occ);
+  if (st != PAD_OK) return st;
+  int64_t parts;
+  if (num_splits <= 0) {
+    parts = (int64_t)sms * occ;
+    if (parts > tiles_ub) parts = tiles_ub;
+  } else {
+    parts = num_splits * batch * hkv;
+    if (parts > (int64_t)1 << 30) return fail(PAD_ERR_UNSUPPORTED, "num_splits %lld too large", (long long)num_splits);
+  }
+  if (parts < 1) parts = 1;
+  plan->partitions = parts;
+  plan->slots = parts + batch * hkv;
+  plan->off_meta = 0;
+  plan->off_ml = align_up((size_t)parts * sizeof(int4), 256);
+  plan->off_o = align_up(plan->off_ml + (size_t)plan->slots * gqa * sizeof(float2), 256);
+  plan->bytes = align_up(plan->off_o + (size_t)plan->slots * gqa * head_dim * sizeof(float), 256);
+  return PAD_OK;
+}
+
+// ----------------------------------------------------------------- tensor maps
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+CUtensorMapSwizzle swizzle_mode(const Instance& in) {
+  if (!in.swz) return CU_TENSOR_MAP_SWIZZLE_NONE;
+  return in.segw == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                        : (in.segw == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+}
+
+int encode_map(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
+               const cuuint32_t* box, CUtensorMapSwizzle swz, const char* what) {
+  auto enc = get_encode();
+  if (enc == nullptr) return fail(PAD_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<void*>(base), dims, strides_bytes, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PAD_ERR_INVALID_ARGUMENT, "cuTensorMapEncodeTiled(%s) failed (%d)", what, (int)r);
+  return PAD_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+// =============================================================================
+extern "C" {
+
+const char* pad_status_string(int status) {
+  switch (status) {
+    case PAD_OK: return "ok";
+    case PAD_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case PAD_ERR_UNSUPPORTED: return "unsupported configuration";
+    case PAD_ERR_WORKSPACE: return "workspace missing or too small";
+    case PAD_ERR_CUDA: return "CUDA error";
+    default: return "unknown status";
+  }
+}
+
+const char* pad_last_error(void) { return g_last_error.c_str(); }
+
+int pad_version(void) { return 100; }
+
+int pad_device_info(int device, int64_t head_dim, int64_t gqa_ratio, int* num_sms, int* ctas_per_sm) {
+  if (num_sms == nullptr || ctas_per_sm == nullptr) return fail(PAD_ERR_INVALID_ARGUMENT, "null output pointer");
+  Instance in;
+  if (gqa_ratio < 1 || gqa_ratio > 16 || !pick_instance(head_dim, gqa_ratio, true, &in))
+    return fail(PAD_ERR_UNSUPPORTED, "no kernel for head_dim %lld gqa %lld", (long long)head_dim,
+                (long long)gqa_ratio);
+  return prepare_device(device, in, instance_key(head_dim, gqa_ratio, true), num_sms, ctas_per_sm);
+}
+
+int pad_decode_partitions(int device, int64_t batch, int64_t num_kv_heads, int64_t gqa_ratio, int64_t head_dim,
+                          int64_t page_size, int64_t max_pages_per_seq, int64_t num_splits, int64_t* partitions) {
+  if (partitions == nullptr) return fail(PAD_ERR_INVALID_ARGUMENT, "null output pointer");
+  Plan plan;
+  int st = make_plan(device, batch, num_kv_heads, gqa_ratio, head_dim, page_size, max_pages_per_seq, num_splits, &plan);
+  if (st == PAD_OK) *partitions = plan.partitions;
+  return st;
+}
+
+int pad_decode_workspace_bytes(int device, int64_t batch, int64_t num_kv_heads, int64_t gqa_ratio, int64_t head_dim,
+                               int64_t page_size, int64_t max_pages_per_seq, int64_t num_splits, size_t* bytes) {
+  if (bytes == nullptr) return fail(PAD_ERR_INVALID_ARGUMENT, "null output pointer");
+  Plan plan;
+  int st = make_plan(device, batch, num_kv_heads, gqa_ratio, head_dim, page_size, max_pages_per_seq, num_splits, &plan);
+  if (st == PAD_OK) *bytes = plan.bytes;
+  return st;
+}
+
+int pad_paged_attention_decode(const void* q, const void* k_cache, const void* v_cache, const int32_t* block_table,
+                               const int32_t* seq_lens, void* out, int64_t batch, int64_t num_q_heads,
+                               int64_t num_kv_heads, int64_t head_dim, int64_t num_pages, int64_t page_size,
+                               int64_t max_pages_per_seq, const int64_t* q_strides, const int64_t* k_strides,
+                               const int64_t* v_strides, int64_t block_table_stride, const int64_t* out_strides,
+                               float scale, int64_t num_splits, void* workspace, size_t workspace_bytes, void* stream,
+                               int32_t* error_flags) {
+  // ---- shape-only checks (no device access, no sync)
+  if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || num_pages < 0 || page_size <= 0 ||
+      max_pages_per_seq < 0)
+    return fail(PAD_ERR_INVALID_ARGUMENT, "negative or zero size");
+  if (num_q_heads % num_kv_heads != 0)
+    return fail(PAD_ERR_INVALID_ARGUMENT, "num_q_heads (%lld) must be divisible by num_kv_heads (%lld)",
+                (long long)num_q_heads, (long long)num_kv_heads);
+  if (q_strides == nullptr || k_strides == nullptr || v_strides == nullptr || out_strides == nullptr)
+    return fail(PAD_ERR_INVALID_ARGUMENT, "null stride array");
+  if (!std::isfinite(scale)) return fail(PAD_ERR_INVALID_ARGUMENT, "scale must be finite");
+  const int64_t gqa = num_q_heads / num_kv_heads;
+  if (batch == 0) return PAD_OK;
+  if (q == nullptr || k_cache == nullptr || v_cache == nullptr || block_table == nullptr || seq_lens == nullptr ||
+      out == nullptr)
+    return fail(PAD_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (q_strides[2] != 1 || k_strides[3] != 1 || v_strides[3] != 1 || out_strides[2] != 1)
+    return fail(PAD_ERR_UNSUPPORTED, "the head_dim axis of q, k_cache, v_cache and out must be contiguous");
+  for (int i = 0; i < 3; ++i)
+    if ((k_strides[i] % 8) || (v_strides[i] % 8) || k_strides[i] <= 0 || v_strides[i] <= 0)
+      return fail(PAD_ERR_UNSUPPORTED, "k_cache/v_cache strides must be positive multiples of 8 elements");
+  if ((q_strides[0] % 8) || (q_strides[1] % 8) || q_strides[0] <= 0 || q_strides[1] <= 0)
+    return fail(PAD_ERR_UNSUPPORTED, "q strides must be positive multiples of 8 elements");
+  if ((out_strides[0] % 2) || (out_strides[1] % 2))
+    return fail(PAD_ERR_UNSUPPORTED, "out strides must be even");
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out))
+    return fail(PAD_ERR_UNSUPPORTED, "q, k_cache, v_cache and out must be 16-byte aligned");
+  if (max_pages_per_seq > 0 && block_table_stride < max_pages_per_seq)
+    return fail(PAD_ERR_INVALID_ARGUMENT, "block_table row stride smaller than its width");
+  if (num_pages == 0 || max_pages_per_seq == 0) {
+    // Nothing addressable: every sequence must be empty. Zero the output.
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    for (int64_t b = 0; b < batch; ++b) {
+      cudaError_t e = cudaMemset2DAsync(static_cast<__half*>(out) + b * out_strides[0], out_strides[1] * 2, 0,
+                                        head_dim * 2, num_q_heads, s);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMemset2DAsync");
+    }
+    return PAD_OK;
+  }
+  if (num_pages > INT32_MAX) return fail(PAD_ERR_UNSUPPORTED, "num_pages exceeds int32");
+
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  Plan plan;
+  int st = make_plan(device, batch, num_kv_heads, gqa, head_dim, page_size, max_pages_per_seq, num_splits, &plan);
+  if (st != PAD_OK) return st;
+  if (workspace == nullptr || workspace_bytes < plan.bytes)
+    return fail(PAD_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", plan.bytes,
+                workspace == nullptr ? (size_t)0 : workspace_bytes);
+  if (!aligned16(workspace)) return fail(PAD_ERR_WORKSPACE, "workspace must be 16-byte aligned");
+
+  DecodeParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  const Instance& in = plan.inst;
+  const CUtensorMapSwizzle swz = swizzle_mode(in);
+  {
+    const cuuint64_t dims[4] = {(cuuint64_t)head_dim, (cuuint64_t)num_kv_heads, (cuuint64_t)page_size,
+                                (cuuint64_t)num_pages};
+    const cuuint32_t box[4] = {(cuuint32_t)(in.segw / 2), 1u, (cuuint32_t)plan.box_rows, 1u};
+    const cuuint64_t ks[3] = {(cuuint64_t)k_strides[2] * 2, (cuuint64_t)k_strides[1] * 2,
+                              (cuuint64_t)k_strides[0] * 2};
+    const cuuint64_t vs[3] = {(cuuint64_t)v_strides[2] * 2, (cuuint64_t)v_strides[1] * 2,
+                              (cuuint64_t)v_strides[0] * 2};
+    if ((st = encode_map(&prm.tm_k, k_cache, 4, dims, ks, box, swz, "k_cache")) != PAD_OK) return st;
+    if ((st = encode_map(&prm.tm_v, v_cache, 4, dims, vs, box, swz, "v_cache")) != PAD_OK) return st;
+  }
+  {
+    const cuuint64_t dims[3] = {(cuuint64_t)head_dim, (cuuint64_t)num_q_heads, (cuuint64_t)batch};
+    const cuuint32_t box[3] = {(cuuint32_t)(in.segw / 2), (cuuint32_t)gqa, 1u};
+    const cuuint64_t qs[2] = {(cuuint64_t)q_strides[1] * 2, (cuuint64_t)q_strides[0] * 2};
+    if ((st = encode_map(&prm.tm_q, q, 3, dims, qs, box, swz, "q")) != PAD_OK) return st;
+  }
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  prm.block_table = block_table;
+  prm.seq_lens = seq_lens;
+  prm.out = static_cast<__half*>(out);
+  prm.ws_meta = reinterpret_cast<int4*>(ws + plan.off_meta);
+  prm.ws_ml = reinterpret_cast<float2*>(ws + plan.off_ml);
+  prm.ws_o = reinterpret_cast<float*>(ws + plan.off_o);
+  prm.error_flags = error_flags;
+  prm.bt_stride = block_table_stride;
+  prm.out_sb = out_strides[0];
+  prm.out_sh = out_strides[1];
+  prm.batch = (int)batch;
+  prm.hkv = (int)num_kv_heads;
+  prm.gqa = (int)gqa;
+  prm.page_size = (int)page_size;
+  prm.num_pages = (int)num_pages;
+  prm.max_pages = (int)max_pages_per_seq;
+  prm.box_rows = plan.box_rows;
+  prm.scale_log2 = scale * kLog2e;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  void* args[] = {&prm};
+  e = cudaLaunchKernel(in.kernel, dim3((unsigned)plan.partitions), dim3(kThreads), args, (size_t)in.smem_bytes, s);
+  if (e != cudaSuccess) return cuda_fail(e, "launching the decode kernel");
+  if (plan.partitions > 1) {
+    const float* a0 = prm.ws_o;
+    const float2* a1 = prm.ws_ml;
+    const int4* a2 = prm.ws_meta;
+    __half* a3 = prm.out;
+    void* margs[] = {&a0, &a1, &a2, &a3, &prm.out_sb, &prm.out_sh, &prm.hkv, &prm.gqa};
+    e = cudaLaunchKernel(in.merge, dim3((unsigned)plan.partitions, (unsigned)gqa), dim3(256), margs, 0, s);
+    if (e != cudaSuccess) return cuda_fail(e, "launching the merge kernel");
+  }
+  return PAD_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,546 @@
+// pad_decode_kernels.cuh -- the two decode kernels (see pad_decode_kernel.cuh
+// for the design summary and the shared definitions).
+#pragma once
+
+#include "pad_b200.h"
+#include "pad_decode_kernel.cuh"
+
+namespace pad {
+
+__device__ __forceinline__ void raise_flag(const DecodeParams& p, int bits) {
+  if (p.error_flags != nullptr) atomicOr(p.error_flags, bits);
+}
+
+// Page ids of the TMA boxes of the tile at cursor `c`: lane j loads box j (and
+// j + 32 when a tile has more than 32 boxes). Boxes past seq_len get id 0 and
+// are never issued.
+template <class TR>
+__device__ __forceinline__ void load_page_ids(const DecodeParams& p, const Cursor& c, int lane, int (&dst)[2]) {
+  const int R = p.box_rows;
+  const int64_t row = (int64_t)c.b * p.bt_stride;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int j = lane + 32 * u;
+    dst[u] = 0;
+    if (TR::NB_MAX > 32 || u == 0) {
+      const int tok = c.i * kTile + j * R;
+      if (j * R < kTile && tok < c.seq) dst[u] = __ldg(p.block_table + row + tok / p.page_size);
+    }
+  }
+}
+
+// Cross-warp epilogue sync on an mbarrier (count = consumer warps) with a
+// bounded wait. Returns false on timeout.
+__device__ __forceinline__ bool epi_sync(uint64_t* bar, uint32_t& phase, int lane) {
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar);
+  const bool ok = mbar_wait_bounded(bar, phase, kWaitTimeoutNs);
+  phase ^= 1u;
+  __syncwarp();
+  return ok;
+}
+
+template <class TR>
+__global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid_constant__ DecodeParams p) {
+  constexpr int D = TR::D, NT = TR::NT, S = TR::STAGES, QROWS = TR::QROWS, KSTEPS = D / 16;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  float* epi = reinterpret_cast<float*>(smem + S * TR::STAGE_BYTES);  // [2][QROWS][D]
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi + 2 * QROWS * D);
+  uint64_t* empty = full + S;
+  uint64_t* ebar = empty + S;
+  TileDesc* descs = reinterpret_cast<TileDesc*>(ebar + 2);
+  int* ids = reinterpret_cast<int*>(descs + S);             // [S][NB_MAX]
+  float2* sml = reinterpret_cast<float2*>(ids + S * TR::NB_MAX);  // [warps][QROWS]
+  float2* sML = sml + kConsumerWarps * QROWS;                   // [QROWS]
+  int* scan = reinterpret_cast<int*>(sML + QROWS);              // [8]
+  volatile int* abort_flag = scan + 8;
+  int* cur_smem = scan + 12;                                    // Cursor as 6 ints
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int cap = p.max_pages * p.page_size;
+  const int64_t W = gridDim.x;
+  const int w = blockIdx.x;
+  const int G = p.gqa;
+
+  // ---- set-up: zero the Q tiles (rows >= G stay zero), init barriers
+  for (int s = 0; s < S; ++s) {
+    uint4* qz = reinterpret_cast<uint4*>(stages + s * TR::STAGE_BYTES + 2 * TR::KT_BYTES);
+    for (int x = tid; x < TR::Q_BYTES / 16; x += kThreads) qz[x] = make_uint4(0, 0, 0, 0);
+  }
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    mbar_init(&ebar[0], kConsumerWarps);
+    *abort_flag = 0;
+    cur_smem[0] = -1;
+    fence_mbar_init();
+  }
+
+  // ---- block-wide exclusive scan of tiles per sequence (x Hkv)
+  const int per = (p.batch + kThreads - 1) / kThreads;
+  const int b_lo = min(p.batch, tid * per), b_hi = min(p.batch, b_lo + per);
+  int local = 0, bad = 0;
+  for (int b = b_lo; b < b_hi; ++b) {
+    const int raw = __ldg(p.seq_lens + b);
+    bad |= (raw < 0 || raw > cap);
+    local += tiles_of(clamp_seq(raw, cap));
+  }
+  local *= p.hkv;
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) scan[warp] = incl;
+  __syncthreads();
+  int excl = incl - local, total = 0;
+  for (int x = 0; x < kThreads / 32; ++x) {
+    const int v = scan[x];
+    if (x < warp) excl += v;
+    total += v;
+  }
+  if (bad && w == 0 && p.error_flags != nullptr) atomicOr(p.error_flags, PAD_FLAG_SEQ_LEN_RANGE);
+  const int t0 = total > 0 ? part_begin(w, total, W) : 0;
+  const int t1 = total > 0 ? part_begin(w + 1, total, W) : 0;
+  if (t0 < total && excl <= t0 && t0 < excl + local) {
+    int acc_t = excl;
+    for (int b = b_lo; b < b_hi; ++b) {
+      const int seq = clamp_seq(__ldg(p.seq_lens + b), cap);
+      const int n = tiles_of(seq);
+      const int tb = n * p.hkv;
+      if (t0 < acc_t + tb) {
+        const int o = t0 - acc_t;
+        cur_smem[0] = b;
+        cur_smem[1] = o / n;
+        cur_smem[2] = o % n;
+        cur_smem[3] = n;
+        cur_smem[4] = seq;
+        cur_smem[5] = acc_t + (o / n) * n;
+        break;
+      }
+      acc_t += tb;
+    }
+  }
+  fence_proxy_async_smem();  // zeroed Q tiles before any TMA write into the stages
+  __syncthreads();
+
+  // ---- zero output rows of empty sequences (src/reference.py:32-34)
+  for (int b = w; b < p.batch; b += (int)W) {
+    if (clamp_seq(__ldg(p.seq_lens + b), cap) == 0) {
+      const int hq = p.hkv * G;
+      for (int x = tid; x < hq * (D / 2); x += kThreads) {
+        const int hh = x / (D / 2), d = (x % (D / 2)) * 2;
+        *reinterpret_cast<__half2*>(p.out + b * p.out_sb + hh * p.out_sh + d) = __floats2half2_rn(0.f, 0.f);
+      }
+    }
+  }
+
+  const int ntiles = t1 - t0;
+
+  if (warp == kConsumerWarps) {
+    // =============================== producer warp ===============================
+    if (lane == 0) p.ws_meta[w] = make_int4(-1, 0, 0, 0);
+    if (ntiles <= 0) {
+      // An empty partition (more partitions than tiles) can sit between the
+      // first and last partition of a split pair; it owns a partial slot of
+      // that pair, which it marks empty (m = -inf, l = 0).
+      if (cur_smem[0] >= 0 && cur_smem[5] < t0) {
+        const int slot = cur_smem[0] * p.hkv + cur_smem[1] + w;
+        for (int g = lane; g < G; g += 32) p.ws_ml[(int64_t)slot * G + g] = make_float2(-INFINITY, 0.f);
+      }
+      return;
+    }
+    const int R = p.box_rows;
+    Cursor c{cur_smem[0], cur_smem[1], cur_smem[2], cur_smem[3], cur_smem[4], cur_smem[5]};
+    Cursor la = c;
+    int pid[S][2];
+#pragma unroll
+    for (int k = 0; k < S; ++k) {
+      pid[k][0] = pid[k][1] = 0;
+      if (k < ntiles) {
+        load_page_ids<TR>(p, la, lane, pid[k]);
+        cursor_next(la, p, cap);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < S; ++k) {
+      if (lane < TR::NB_MAX) ids[k * TR::NB_MAX + lane] = pid[k][0];
+      if constexpr (TR::NB_MAX > 32) ids[k * TR::NB_MAX + 32 + lane] = pid[k][1];
+    }
+    __syncwarp();
+    int pend[2] = {0, 0};
+    bool have_pend = false;
+    int issued = 0;
+    bool ok = true;
+    for (int k = 0; k < ntiles; ++k) {
+      const int s = k % S;
+      if (k >= S) {
+        if (!mbar_wait_bounded(&empty[s], ((k / S) - 1) & 1, kWaitTimeoutNs)) ok = false;
+        if (__any_sync(0xffffffffu, !ok) || *abort_flag) {
+          ok = false;
+          break;
+        }
+      }
+      if (have_pend) {
+        const int ps = (k - 1) % S;
+        if (lane < TR::NB_MAX) ids[ps * TR::NB_MAX + lane] = pend[0];
+        if constexpr (TR::NB_MAX > 32) ids[ps * TR::NB_MAX + 32 + lane] = pend[1];
+        have_pend = false;
+      }
+      __syncwarp();
+      const int tok0 = c.i * kTile;
+      const int vt = min(kTile, c.seq - tok0);
+      const int nvalid = (vt + R - 1) / R;
+      const bool first = (k == 0) || (c.i == 0);
+      const bool last = (k == ntiles - 1) || (c.i == c.n - 1);
+      const int pair = c.b * p.hkv + c.h;
+      const bool split = !(c.pair_start >= t0 && c.pair_start + c.n <= t1);
+      if (lane == 0) {
+        TileDesc dsc;
+        dsc.b = c.b;
+        dsc.h = c.h;
+        dsc.i = c.i;
+        dsc.seq = c.seq;
+        dsc.flags = (first ? kFirst : 0) | (last ? kLast : 0) | (split ? kSplit : 0);
+        // Partial slots: pair p uses slots [p + owner(start_p), ...], one per
+        // partition touching it; partition w writes slot p + w. These ranges
+        // are disjoint across pairs and never exceed partitions + pairs.
+        dsc.slot = pair + w;
+        dsc.pad0 = dsc.pad1 = 0;
+        descs[s] = dsc;
+        if (split && c.i == 0 && first) {
+          const int last_owner = part_owner((int64_t)c.pair_start + c.n - 1, total, W);
+          p.ws_meta[w] = make_int4(pair, pair + w, last_owner - w + 1, 1);
+        }
+        const uint32_t bytes = (uint32_t)nvalid * R * TR::ROW_BYTES * 2 + (first ? (uint32_t)G * TR::ROW_BYTES : 0u);
+        mbar_arrive_expect_tx(&full[s], bytes);
+      }
+      __syncwarp();
+      uint8_t* st = stages + s * TR::STAGE_BYTES;
+      for (int j = lane; j < nvalid; j += 32) {
+        const int page = ids[s * TR::NB_MAX + j];
+        if ((unsigned)page >= (unsigned)p.num_pages) raise_flag(p, PAD_FLAG_BAD_PAGE_ID);
+        const int row = (tok0 + j * R) % p.page_size;
+#pragma unroll
+        for (int sg = 0; sg < TR::NSEG; ++sg) {
+          const int off = sg * kTile * TR::SEGW + j * (int)TR::box_pitch(R);
+          tma_load_4d(st + off, &p.tm_k, &full[s], sg * (TR::SEGW / 2), c.h, row, page);
+          tma_load_4d(st + TR::KT_BYTES + off, &p.tm_v, &full[s], sg * (TR::SEGW / 2), c.h, row, page);
+        }
+      }
+      if (first && lane == 0) {
+#pragma unroll
+        for (int sg = 0; sg < TR::NSEG; ++sg)
+          tma_load_3d(st + 2 * TR::KT_BYTES + sg * QROWS * TR::SEGW, &p.tm_q, &full[s], sg * (TR::SEGW / 2), c.h * G,
+                      c.b);
+      }
+      ++issued;
+      if (k + S < ntiles) {
+        load_page_ids<TR>(p, la, lane, pend);
+        cursor_next(la, p, cap);
+        have_pend = true;
+      }
+      cursor_next(c, p, cap);
+    }
+    if (!ok) {
+      // Unwind: record the failure, stop the consumers, and wait (bounded)
+      // for this CTA's own copies still in flight before exiting.
+      if (lane == 0) {
+        raise_flag(p, PAD_FLAG_WAIT_TIMEOUT);
+        *abort_flag = 1;
+        for (int k = max(0, issued - S); k < issued; ++k)
+          (void)mbar_wait_bounded(&full[k % S], (k / S) & 1, kWaitTimeoutNs / 4);
+      }
+    }
+    return;
+  }
+
+  // =============================== consumer warps ===============================
+  if (ntiles <= 0) return;
+  const int gl = 2 * (lane & 3);  // first query row (within an n8 tile) this lane owns
+  uint32_t qf[KSTEPS][NT][2];
+  float acc[KSTEPS][NT][4];
+  float m_run[NT][2], l_run[NT][2];
+  uint32_t ephase = 0;
+  const uint32_t r0 = warp * 16;
+
+  for (int k = 0; k < ntiles; ++k) {
+    const int s = k % S;
+    bool ok = mbar_wait_bounded(&full[s], (k / S) & 1, kWaitTimeoutNs);
+    if (!__all_sync(0xffffffffu, ok) || *abort_flag) {
+      if (lane == 0) {
+        raise_flag(p, PAD_FLAG_WAIT_TIMEOUT);
+        *abort_flag = 1;
+      }
+      return;
+    }
+    const TileDesc dsc = descs[s];
+    const uint32_t kb = smem_u32(stages + s * TR::STAGE_BYTES);
+    const uint32_t vb = kb + TR::KT_BYTES;
+    const uint32_t qb = kb + 2 * TR::KT_BYTES;
+
+    if (dsc.flags & kFirst) {
+      if constexpr (KSTEPS == 1) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+          ldsm_x2(TR::q_addr(qb, nt * 8 + (lane & 7), (lane >> 3) & 1), qf[0][nt][0], qf[0][nt][1]);
+      } else {
+#pragma unroll
+        for (int kk = 0; kk < KSTEPS; kk += 2)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+            ldsm_x4(TR::q_addr(qb, nt * 8 + (lane & 7), kk * 2 + (lane >> 3)), qf[kk][nt][0],
+                    qf[kk][nt][1], qf[kk + 1][nt][0], qf[kk + 1][nt][1]);
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        m_run[nt][0] = m_run[nt][1] = -INFINITY;
+        l_run[nt][0] = l_run[nt][1] = 0.f;
+#pragma unroll
+        for (int mt = 0; mt < KSTEPS; ++mt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[mt][nt][e] = 0.f;
+      }
+    }
+
+    const int nv = min(16, dsc.seq - (dsc.i * kTile + (int)r0));
+    if (nv > 0) {
+      if (nv < 16) {
+        // Rows past seq_len hold whatever the page (or an earlier tile) left
+        // there -- possibly NaN/Inf. Zero this warp's V rows so 0-probability
+        // tokens contribute exactly 0; K rows are masked through the scores.
+        for (int x = lane; x < (16 - nv) * (D / 8); x += 32) {
+          const uint32_t row = r0 + nv + x / (D / 8), cc = x % (D / 8);
+          asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(TR::kv_addr(vb, row, cc, p.box_rows)), "r"(0)
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+      }
+      // S^T[16 tokens x 8*NT rows] = K[16 x D] . Q^T
+      float sc[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < KSTEPS; ++kk) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(TR::kv_addr(kb, r0 + (lane & 7) + ((lane >> 3) & 1) * 8, kk * 2 + (lane >> 4), p.box_rows), a0, a1,
+                a2, a3);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma_16816(sc[nt], a0, a1, a2, a3, qf[kk][nt][0], qf[kk][nt][1]);
+      }
+      // scale into log2 units, mask tokens past seq_len
+      const bool v_lo = (lane >> 2) < nv, v_hi = (lane >> 2) + 8 < nv;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        sc[nt][0] = v_lo ? sc[nt][0] * p.scale_log2 : -INFINITY;
+        sc[nt][1] = v_lo ? sc[nt][1] * p.scale_log2 : -INFINITY;
+        sc[nt][2] = v_hi ? sc[nt][2] * p.scale_log2 : -INFINITY;
+        sc[nt][3] = v_hi ? sc[nt][3] * p.scale_log2 : -INFINITY;
+      }
+      // online softmax (per query row, over this warp's tokens)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          float mx = fmaxf(sc[nt][j], sc[nt][j + 2]);
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+          const float mn = fmaxf(m_run[nt][j], mx);
+          const float mu = (mn == -INFINITY) ? 0.f : mn;
+          const float alpha = ex2(m_run[nt][j] - mu);
+          const float p0 = ex2(sc[nt][j] - mu), p1 = ex2(sc[nt][j + 2] - mu);
+          sc[nt][j] = p0;
+          sc[nt][j + 2] = p1;
+          l_run[nt][j] = l_run[nt][j] * alpha + p0 + p1;
+          m_run[nt][j] = mn;
+#pragma unroll
+          for (int mt = 0; mt < KSTEPS; ++mt) {
+            acc[mt][nt][j] *= alpha;
+            acc[mt][nt][j + 2] *= alpha;
+          }
+        }
+      }
+      // P^T as the B operand: fp16 pack, then transpose 8x8 blocks in registers
+      uint32_t pb[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        pb[nt][0] = movmatrix_trans(pack_half2(sc[nt][0], sc[nt][1]));
+        pb[nt][1] = movmatrix_trans(pack_half2(sc[nt][2], sc[nt][3]));
+      }
+      // O^T[D x 8*NT] += V^T[D x 16 tokens] . P^T
+#pragma unroll
+      for (int mt = 0; mt < KSTEPS; ++mt) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_trans(TR::kv_addr(vb, r0 + (lane & 7) + ((lane >> 4) & 1) * 8, mt * 2 + ((lane >> 3) & 1), p.box_rows),
+                      a0, a1, a2, a3);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma_16816(acc[mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+
+    if (dsc.flags & kLast) {
+      // ---------------- segment epilogue: merge the 4 warps, write out / partial
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          float l = l_run[nt][j];
+          l += __shfl_xor_sync(0xffffffffu, l, 4);
+          l += __shfl_xor_sync(0xffffffffu, l, 8);
+          l += __shfl_xor_sync(0xffffffffu, l, 16);
+          l_run[nt][j] = l;
+          if ((lane >> 2) == 0) sml[warp * QROWS + nt * 8 + gl + j] = make_float2(m_run[nt][j], l);
+        }
+      bool eok = epi_sync(&ebar[0], ephase, lane);
+      float scl[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int g = nt * 8 + gl + j;
+          float M = -INFINITY;
+#pragma unroll
+          for (int ww = 0; ww < kConsumerWarps; ++ww) M = fmaxf(M, sml[ww * QROWS + g].x);
+          const float Mu = (M == -INFINITY) ? 0.f : M;
+          float L = 0.f;
+#pragma unroll
+          for (int ww = 0; ww < kConsumerWarps; ++ww) {
+            const float2 x = sml[ww * QROWS + g];
+            L += x.y * ex2(x.x - Mu);
+          }
+          scl[nt][j] = ex2(m_run[nt][j] - Mu);
+          if (warp == 0 && (lane >> 2) == 0) sML[g] = make_float2(Mu, L);
+        }
+      // warps 0,1 store their scaled O^T into two buffers, then warps 2,3 add
+      float* buf = epi + (warp & 1) * QROWS * D;
+#pragma unroll
+      for (int half_pass = 0; half_pass < 2; ++half_pass) {
+        if ((warp >> 1) == half_pass) {
+#pragma unroll
+          for (int mt = 0; mt < KSTEPS; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int d = mt * 16 + (lane >> 2) + (e >= 2 ? 8 : 0);
+                const int g = nt * 8 + gl + (e & 1);
+                const float v = acc[mt][nt][e] * scl[nt][e & 1];
+                if (half_pass == 0) buf[g * D + d] = v;
+                else buf[g * D + d] += v;
+              }
+        }
+        eok &= epi_sync(&ebar[0], ephase, lane);
+      }
+      const int ctid = warp * 32 + lane;
+      if (!(dsc.flags & kSplit)) {
+        __half* orow = p.out + dsc.b * p.out_sb + (int64_t)(dsc.h * G) * p.out_sh;
+        for (int x = ctid; x < G * (D / 2); x += 32 * kConsumerWarps) {
+          const int g = x / (D / 2), d = (x % (D / 2)) * 2;
+          const float L = sML[g].y;
+          const float inv = L > 0.f ? 1.f / L : 0.f;
+          const float v0 = epi[g * D + d] + epi[QROWS * D + g * D + d];
+          const float v1 = epi[g * D + d + 1] + epi[QROWS * D + g * D + d + 1];
+          *reinterpret_cast<__half2*>(orow + g * p.out_sh + d) = __floats2half2_rn(v0 * inv, v1 * inv);
+        }
+      } else {
+        float4* o4 = reinterpret_cast<float4*>(p.ws_o + (int64_t)dsc.slot * G * D);
+        for (int x = ctid; x < G * (D / 4); x += 32 * kConsumerWarps) {
+          const int g = x / (D / 4), d = (x % (D / 4)) * 4;
+          const float4 a = *reinterpret_cast<const float4*>(epi + g * D + d);
+          const float4 bq = *reinterpret_cast<const float4*>(epi + QROWS * D + g * D + d);
+          o4[x] = make_float4(a.x + bq.x, a.y + bq.y, a.z + bq.z, a.w + bq.w);
+        }
+        if (ctid < G) p.ws_ml[(int64_t)dsc.slot * G + ctid] = sML[ctid];
+      }
+      eok &= epi_sync(&ebar[0], ephase, lane);
+      if (!eok) {
+        if (lane == 0) {
+          raise_flag(p, PAD_FLAG_WAIT_TIMEOUT);
+          *abort_flag = 1;
+        }
+        return;
+      }
+    }
+  }
+}
+
+// Phase 2: merge the partials of one split (sequence, KV head) pair for one
+// query row. Grid (partitions, G); partition w works only if it is the first
+// partition of a split pair (ws_meta[w].w == 1).
+//   M = max_s m_s;  L = sum_s l_s 2^(m_s - M);  O = sum_s O_s 2^(m_s - M) / L
+// (analysis/split_k_derivation.md:44-65; a partial with m_s = -inf weighs 0,
+// the guard of analysis/split_k_derivation.md:67-86).
+template <int D>
+__global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ ws_o, const float2* __restrict__ ws_ml,
+                                                    const int4* __restrict__ ws_meta, __half* __restrict__ out,
+                                                    int64_t out_sb, int64_t out_sh, int hkv, int G) {
+  constexpr int C4 = D / 4;
+  constexpr int SG = 256 / C4;
+  __shared__ float red[SG][D];
+  __shared__ float lred[SG];
+  __shared__ float wmax[8];
+  const int w = blockIdx.x, g = blockIdx.y, tid = threadIdx.x;
+  const int4 meta = ws_meta[w];
+  if (meta.w != 1) return;
+  const int pair = meta.x, s0 = meta.y, ns = meta.z;
+  // pass 1: the running max over partials
+  float mx = -INFINITY;
+  for (int s = tid; s < ns; s += 256) mx = fmaxf(mx, ws_ml[(int64_t)(s0 + s) * G + g].x);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((tid & 31) == 0) wmax[tid >> 5] = mx;
+  __syncthreads();
+  float M = wmax[0];
+#pragma unroll
+  for (int x = 1; x < 8; ++x) M = fmaxf(M, wmax[x]);
+  const float Mu = (M == -INFINITY) ? 0.f : M;
+  // pass 2: weighted sums, partials strided over SG groups
+  const int c = tid % C4, sg = tid / C4;
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+  float lsum = 0.f;
+#pragma unroll 4
+  for (int s = sg; s < ns; s += SG) {
+    const int64_t row = (int64_t)(s0 + s) * G + g;
+    const float2 ml = ws_ml[row];
+    if (ml.x == -INFINITY) continue;  // an empty partial: weight 0, its O is not read
+    const float wt = ex2(ml.x - Mu);
+    const float4 o = reinterpret_cast<const float4*>(ws_o + row * D)[c];
+    lsum += ml.y * wt;
+    a.x += o.x * wt;
+    a.y += o.y * wt;
+    a.z += o.z * wt;
+    a.w += o.w * wt;
+  }
+  *reinterpret_cast<float4*>(&red[sg][c * 4]) = a;
+  if (c == 0) lred[sg] = lsum;
+  __syncthreads();
+  if (tid < C4) {
+    float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+    float L = 0.f;
+#pragma unroll
+    for (int x = 0; x < SG; ++x) {
+      const float4 v = *reinterpret_cast<const float4*>(&red[x][tid * 4]);
+      t.x += v.x;
+      t.y += v.y;
+      t.z += v.z;
+      t.w += v.w;
+      L += lred[x];
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    const int b = pair / hkv, h = pair % hkv;
+    __half* o = out + b * out_sb + (int64_t)(h * G + g) * out_sh + tid * 4;
+    reinterpret_cast<__half2*>(o)[0] = __floats2half2_rn(t.x * inv, t.y * inv);
+    reinterpret_cast<__half2*>(o)[1] = __floats2half2_rn(t.z * inv, t.w * inv);
+  }
+}
+
+}  // namespace pad

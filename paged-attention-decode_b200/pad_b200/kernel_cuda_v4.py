@@ -1,0 +1,174 @@
+"""Drop-in replacement for the reference's ``src/kernel_cuda_v4.py``.
+
+``paged_attention_decode_cuda_v4(q, k_cache, v_cache, block_table, seq_lens,
+num_splits=None, scale=None)`` keeps the reference signature and contract
+(src/kernel_cuda_v4.py:19-65): fp16 CUDA tensors in, a new fp16 ``out``
+shaped like ``q`` back, ``scale=None`` meaning ``1/sqrt(head_dim)``, Python
+``assert`` for the caller-contract checks the reference asserts
+(src/kernel_cuda_v4.py:37-48), ``block_table``/``seq_lens`` cast to int32
+(src/kernel_cuda_v4.py:58-59).
+
+Differences, by design:
+  * ``num_splits=None`` selects the B200 heuristic (one persistent partition
+    per resident CTA slot, stream-K balanced) instead of the reference's
+    fixed 64; an explicit ``num_splits=S`` launches ``S * batch * Hkv``
+    partitions, i.e. S splits per (sequence, KV head) pair for uniform
+    batches, exactly as the reference's grid.z = S did.
+  * The launch goes to the current torch stream of ``q``'s device.
+  * Argument errors the native library detects raise ``PadError``
+    (a RuntimeError, like the reference's TORCH_CHECK).
+  * With ``PAD_B200_CHECK=1`` in the environment the call synchronises and
+    raises ValueError for invalid block-table page ids or out-of-range
+    seq_lens -- the value checks of the reference oracle
+    (src/reference.py:40-41,107-112); off by default because it syncs.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+
+import torch
+
+from . import _lib
+
+_SUPPORTED_HEAD_DIMS = (16, 32, 64, 128)
+_CHECK_VALUES = os.environ.get("PAD_B200_CHECK", "0") not in ("", "0")
+
+
+class _DeviceState:
+    """Per (device, stream) reusable workspace and error-flag word."""
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.workspace = torch.empty(0, dtype=torch.uint8, device=device)
+        self.flags = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def workspace_ptr(self, nbytes: int) -> int:
+        if self.workspace.numel() < nbytes:
+            self.workspace = torch.empty(max(nbytes, 2 * self.workspace.numel()), dtype=torch.uint8,
+                                         device=self.device)
+        return self.workspace.data_ptr()
+
+
+_STATE: dict[tuple[int, int], _DeviceState] = {}
+_WS_CACHE: dict[tuple, int] = {}
+
+
+def _state(device: torch.device, stream: int) -> _DeviceState:
+    key = (device.index, stream)
+    st = _STATE.get(key)
+    if st is None:
+        st = _STATE[key] = _DeviceState(device)
+    return st
+
+
+def workspace_bytes(device_index: int, batch: int, num_kv_heads: int, gqa_ratio: int, head_dim: int,
+                    page_size: int, max_pages: int, num_splits: int) -> int:
+    key = (device_index, batch, num_kv_heads, gqa_ratio, head_dim, page_size, max_pages, num_splits)
+    n = _WS_CACHE.get(key)
+    if n is None:
+        lib = _lib.load()
+        out = _lib.ctypes.c_size_t(0)
+        _lib.check(lib.pad_decode_workspace_bytes(device_index, batch, num_kv_heads, gqa_ratio, head_dim,
+                                                  page_size, max_pages, num_splits, _lib.ctypes.byref(out)))
+        n = _WS_CACHE[key] = int(out.value)
+    return n
+
+
+def partitions(device_index: int, batch: int, num_kv_heads: int, gqa_ratio: int, head_dim: int,
+               page_size: int, max_pages: int, num_splits: int | None = None) -> int:
+    """Number of persistent partitions (CTAs) a call with these sizes launches."""
+    lib = _lib.load()
+    out = _lib.ctypes.c_int64(0)
+    _lib.check(lib.pad_decode_partitions(device_index, batch, num_kv_heads, gqa_ratio, head_dim, page_size,
+                                         max_pages, 0 if num_splits is None else num_splits,
+                                         _lib.ctypes.byref(out)))
+    return int(out.value)
+
+
+def _raise_for_flags(flags: int) -> None:
+    if flags & _lib.PAD_FLAG_BAD_PAGE_ID:
+        raise ValueError("block_table contains an invalid physical page id")
+    if flags & _lib.PAD_FLAG_SEQ_LEN_RANGE:
+        raise ValueError("seq_lens contains negative values or values larger than block_table can address")
+    if flags & _lib.PAD_FLAG_WAIT_TIMEOUT:
+        raise RuntimeError("libpad_b200: an in-kernel wait timed out")
+
+
+def paged_attention_decode_cuda_v4(
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_table: torch.Tensor,
+    seq_lens: torch.Tensor,
+    num_splits: int | None = None,
+    scale: float | None = None,
+    *,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Decode attention over a paged fp16 KV cache with GQA on a B200.
+
+    q [B, Hq, D] fp16, k_cache/v_cache [num_pages, page_size, Hkv, D] fp16,
+    block_table [B, max_pages] int, seq_lens [B] int -> out [B, Hq, D] fp16.
+    """
+    assert q.is_cuda and k_cache.is_cuda and v_cache.is_cuda, "pad_b200 requires CUDA tensors"
+    assert q.dtype == torch.float16 and k_cache.dtype == torch.float16 and v_cache.dtype == torch.float16, (
+        "pad_b200 expects fp16 q/k_cache/v_cache"
+    )
+    assert q.dim() == 3 and k_cache.dim() == 4, "q must be [B, Hq, D] and k_cache [num_pages, page_size, Hkv, D]"
+    assert v_cache.shape == k_cache.shape, "v_cache must have k_cache's shape"
+    batch, num_q_heads, head_dim = q.shape
+    num_pages, page_size, num_kv_heads, cache_head_dim = k_cache.shape
+    assert cache_head_dim == head_dim, "q head_dim must match the KV cache head_dim"
+    assert num_q_heads % num_kv_heads == 0, "num_q_heads must be divisible by num_kv_heads (GQA)"
+    assert head_dim in _SUPPORTED_HEAD_DIMS, f"head_dim must be one of {_SUPPORTED_HEAD_DIMS}"
+    assert block_table.dim() == 2 and block_table.shape[0] == batch, "block_table must be [B, max_pages]"
+    assert seq_lens.dim() == 1 and seq_lens.shape[0] == batch, "seq_lens must be [B]"
+    assert num_splits is None or num_splits >= 1, "num_splits must be >= 1"
+    gqa_ratio = num_q_heads // num_kv_heads
+
+    dev = q.device
+    block_table = block_table.to(device=dev, dtype=torch.int32)
+    if block_table.stride(1) != 1:
+        block_table = block_table.contiguous()
+    seq_lens = seq_lens.to(device=dev, dtype=torch.int32).contiguous()
+    scale = scale if scale is not None else 1.0 / math.sqrt(head_dim)
+    if q.stride(2) != 1 or q.stride(0) % 8 or q.stride(1) % 8 or q.data_ptr() % 16:
+        q = q.contiguous()
+    if out is None:
+        out = torch.empty((batch, num_q_heads, head_dim), dtype=torch.float16, device=dev)
+    else:
+        assert out.shape == q.shape and out.dtype == torch.float16 and out.device == dev, "bad out tensor"
+    if batch == 0:
+        return out
+
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        st = _state(dev, stream)
+        splits = 0 if num_splits is None else int(num_splits)
+        max_pages = block_table.shape[1]
+        nbytes = workspace_bytes(dev.index, batch, num_kv_heads, gqa_ratio, head_dim, page_size, max_pages, splits)
+        ws = st.workspace_ptr(nbytes)
+        lib = _lib.load()
+        if _CHECK_VALUES:
+            st.flags.zero_()
+        _lib.check(lib.pad_paged_attention_decode(
+            q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_table.data_ptr(), seq_lens.data_ptr(),
+            out.data_ptr(), batch, num_q_heads, num_kv_heads, head_dim, num_pages, page_size, max_pages,
+            _lib.i64_array(q.stride()), _lib.i64_array(k_cache.stride()), _lib.i64_array(v_cache.stride()),
+            block_table.stride(0), _lib.i64_array(out.stride()), float(scale), splits, ws, st.workspace.numel(),
+            stream, st.flags.data_ptr()))
+        if _CHECK_VALUES:
+            _raise_for_flags(int(st.flags.item()))
+    return out
+
+
+def read_error_flags(device: torch.device | None = None, reset: bool = True) -> int:
+    """PAD_FLAG_* bits the kernels raised on ``device``'s current stream since the last reset (syncs)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    st = _state(dev, torch.cuda.current_stream(dev).cuda_stream)
+    v = int(st.flags.item())
+    if reset:
+        st.flags.zero_()
+    return v

@@ -1,0 +1,74 @@
+"""Host mirror of the decode kernel's stream-K work partition.
+
+The kernel flattens the batch into one list of 64-token tiles ordered
+(sequence, KV head, tile) and gives partition ``w`` of ``W`` the tiles
+``[floor(w*T/W), floor((w+1)*T/W))``. A (sequence, KV head) pair whose tiles
+fall in one partition is finished there; a pair spread over several
+partitions gets one fp32 partial per partition, in slots
+``pair + w`` for ``w`` in ``[owner(first tile), owner(last tile)]``, which the
+merge kernel combines. This module computes the same plan on the host (for
+tests, diagnostics and workspace sizing); it never runs on the decode path.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+TILE = 64
+
+
+def tiles_of(seq: int) -> int:
+    return (max(int(seq), 0) + TILE - 1) // TILE
+
+
+def part_begin(w: int, total: int, parts: int) -> int:
+    return (w * total) // parts
+
+
+def part_owner(t: int, total: int, parts: int) -> int:
+    return ((t + 1) * parts - 1) // total
+
+
+@dataclass
+class PairPlan:
+    pair: int
+    first_tile: int
+    n_tiles: int
+    first_part: int
+    last_part: int
+
+    @property
+    def split(self) -> bool:
+        return self.last_part > self.first_part
+
+    @property
+    def slots(self) -> range:
+        return range(self.pair + self.first_part, self.pair + self.last_part + 1)
+
+
+def plan(seq_lens, num_kv_heads: int, parts: int, cap: int | None = None) -> tuple[int, list[PairPlan]]:
+    """Return (total tiles, per-pair plan) for ``parts`` partitions."""
+    seq = np.asarray(seq_lens, dtype=np.int64)
+    if cap is not None:
+        seq = np.clip(seq, 0, cap)
+    total = int(sum(tiles_of(s) for s in seq) * num_kv_heads)
+    pairs: list[PairPlan] = []
+    start = 0
+    for b, s in enumerate(seq):
+        n = tiles_of(s)
+        for h in range(num_kv_heads):
+            if n > 0:
+                pairs.append(PairPlan(b * num_kv_heads + h, start, n, part_owner(start, total, parts),
+                                      part_owner(start + n - 1, total, parts)))
+            start += n
+    return total, pairs
+
+
+def heuristic_partitions(num_sms: int, ctas_per_sm: int, batch: int, num_kv_heads: int, max_pages: int,
+                         page_size: int) -> int:
+    """The num_splits=None choice: one partition per resident CTA slot,
+    capped by the number of tiles the batch can hold."""
+    cap_tiles = batch * num_kv_heads * tiles_of(max_pages * page_size)
+    return max(1, min(num_sms * ctas_per_sm, cap_tiles))

