@@ -1,0 +1,439 @@
+"""Benchmark of the B200 paged-attention decode path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c2|c3|c4|c5]
+
+Prints ONE JSON line on rank 0.
+
+Workload (default ``c2``): BASELINE config 2, the Qwen2.5-1.5B-shaped decode
+(12 Q / 2 KV heads, head_dim 128, page 16, seq 4096, random page permutation)
+at batch 64 -- the largest point of the batch-1..64 sweep the metric is quoted
+on. A step is one decode call over the whole batch. ``value`` is achieved
+KV-read bandwidth in TB/s: algorithmic bytes (sum_b seq_b * Hkv * D * 2 (K,V)
+* 2 B, the reference's bench/roofline.py:55-59 formula) / device time, summed
+over ranks (each rank decodes its own batch: weak scaling, no collective).
+Extra keys give the full batch sweep and the long-context point (config 3,
+batch 1, seq 32768).
+
+Timing: inputs are rotated over independent KV pools whose total exceeds L2
+(126 MB), so every step reads HBM; steps are recorded once into a CUDA graph
+(the per-call host overhead is measured separately in ``e2e``) and replayed;
+CUDA events on the launching stream bracket exactly K steps, with a barrier
+and device synchronisation on both sides; multi-GPU takes the max over ranks.
+``nvidia-smi`` samples clocks during the timed region.
+
+``--impl reference`` times the reference algorithm's CPU implementation -- the
+C restatement of src/reference.py in oracle/ (the reference is Python and
+cannot be compiled) -- on the host cores for the same workload and metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+for _p in (REPO, os.path.join(REPO, "paged-attention-decode_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+
+L2_BYTES = 126 * 2**20
+GRAPH_STEPS = 100  # steps recorded per CUDA graph; the graph is replayed to reach K
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="c2", choices=["c2", "c3", "c4", "c5"])
+    ap.add_argument("--no-sweep", action="store_true", help="skip the batch sweep / long-context extras")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="time the workload only (no e2e, CPU baseline or sweep); used for ncu captures")
+    return ap.parse_args()
+
+
+def workload_spec(name: str, n_gpus: int, rank: int):
+    """(config name, batch, seq_len, seq_lens override) for this rank."""
+    from pad_b200.cases import config_seq_lens
+
+    if name == "c2":
+        return "c2", 64, 4096, None
+    if name == "c3":
+        return "c3", 1, 32768, None
+    if name == "c4":
+        return "c4", 256, None, None
+    if name == "c5":  # batch 1024 split evenly by sequence across the GPUs
+        sl = config_seq_lens("c5")
+        per = len(sl) // n_gpus
+        return "c5", per, None, sl[rank * per:(rank + 1) * per]
+    raise KeyError(name)
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def committed_traffic():
+    """dram bytes per launch of the decode kernel from the committed ncu summary."""
+    path = os.path.join(REPO, "profiles", "decode_stream_kernel_c2_b64.md")
+    if not os.path.exists(path):
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", open(path).read())
+    return float(m.group(1)) if m else None
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.15)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            out, _ = self.proc.communicate(timeout=10)
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        mhz, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            try:
+                mhz.append(float(f[1]))
+                mx = float(f[2])
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not mhz:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+# ------------------------------------------------------------------ our arm
+def make_pools(cfg, batch, seq_len, seq_lens, device, min_bytes):
+    from pad_b200.cases import config_case, kv_bytes
+
+    first = config_case(cfg, batch=batch, seq_len=seq_len, seq_lens=seq_lens, device=device, seed=0)
+    per = kv_bytes(first.seq_lens.cpu().numpy(), first.k_cache.shape[2], first.k_cache.shape[3])
+    n = max(2, min(64, math.ceil(min_bytes / max(per, 1))))
+    pools = [first] + [config_case(cfg, batch=batch, seq_len=seq_len, seq_lens=seq_lens, device=device, seed=i)
+                       for i in range(1, n)]
+    return pools, per
+
+
+def time_device(pools, steps, warmup, torch, barrier):
+    """Device time of `steps` decode calls rotated over `pools` (ms)."""
+    import pad_b200
+
+    stream = torch.cuda.Stream()
+    outs = [torch.empty_like(c.q) for c in pools]
+
+    def call(i):
+        c = pools[i % len(pools)]
+        pad_b200.paged_attention_decode_cuda_v4(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens,
+                                                out=outs[i % len(pools)])
+
+    with torch.cuda.stream(stream):
+        for i in range(max(warmup, len(pools))):
+            call(i)
+    stream.synchronize()
+    g_steps = min(GRAPH_STEPS, steps)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(g_steps):
+            call(i)
+    reps, tail = divmod(steps, g_steps)
+    g_tail = None
+    if tail:
+        g_tail = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_tail, stream=stream):
+            for i in range(tail):
+                call(i)
+    with torch.cuda.stream(stream):
+        g.replay()
+    stream.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(reps):
+            g.replay()
+        if g_tail is not None:
+            g_tail.replay()
+        end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    return start.elapsed_time(end)
+
+
+def time_e2e(pool, steps, torch):
+    """Through the public API with host buffers: per step H2D of every input
+    (q, k_cache, v_cache, block_table, seq_lens) from pinned memory, the
+    decode, and D2H of the output. Returns (ms per step, h2d bytes, d2h bytes)."""
+    import pad_b200
+
+    host = [t.cpu().pin_memory() for t in (pool.q, pool.k_cache, pool.v_cache, pool.block_table, pool.seq_lens)]
+    dev = [torch.empty_like(t, device="cuda") for t in host]
+    out_h = torch.empty(pool.q.shape, dtype=torch.float16).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    d2h = out_h.numel() * out_h.element_size()
+
+    def step():
+        for d, h in zip(dev, host):
+            d.copy_(h, non_blocking=True)
+        o = pad_b200.paged_attention_decode_cuda_v4(*dev)
+        out_h.copy_(o, non_blocking=True)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / steps, h2d, d2h
+
+
+def time_e2e_resident(pool, steps, torch):
+    """KV cache resident in HBM (as in a serving engine); per step H2D of q,
+    block_table and seq_lens, the decode and D2H of the output, Python wrapper
+    and C-ABI call included (no graph)."""
+    import pad_b200
+
+    host = [t.cpu().pin_memory() for t in (pool.q, pool.block_table, pool.seq_lens)]
+    dev = [torch.empty_like(t, device="cuda") for t in host]
+    out_h = torch.empty(pool.q.shape, dtype=torch.float16).pin_memory()
+
+    def step():
+        for d, h in zip(dev, host):
+            d.copy_(h, non_blocking=True)
+        o = pad_b200.paged_attention_decode_cuda_v4(dev[0], pool.k_cache, pool.v_cache, dev[1], dev[2])
+        out_h.copy_(o, non_blocking=True)
+
+    for _ in range(5):
+        step()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / steps, sum(t.numel() * t.element_size() for t in host), \
+        out_h.numel() * out_h.element_size()
+
+
+def cpu_baseline_sample(pool, seconds: float = 10.0):
+    """The C oracle (oracle/pa_oracle.c, the reference algorithm) on the host
+    cores, on a bounded sample of the workload's sequences; TB/s of KV read."""
+    import oracle
+
+    q = pool.q.cpu().numpy()
+    k = pool.k_cache.cpu().numpy()
+    v = pool.v_cache.cpu().numpy()
+    bt = pool.block_table.cpu().numpy()
+    sl = pool.seq_lens.cpu().numpy()
+    threads = oracle.max_threads()
+    n = len(sl)
+    take = n
+    # size the sample so one call takes well under `seconds`
+    probe = min(n, 2)
+    t0 = time.perf_counter()
+    oracle.decode_c(q[:probe], k, v, bt[:probe], sl[:probe], nthreads=threads)
+    dt = max(time.perf_counter() - t0, 1e-4)
+    take = max(1, min(n, int(probe * (seconds / 4) / dt)))
+    calls, elapsed = 0, 0.0
+    t0 = time.perf_counter()
+    while elapsed < seconds and calls < 50:
+        oracle.decode_c(q[:take], k, v, bt[:take], sl[:take], nthreads=threads)
+        calls += 1
+        elapsed = time.perf_counter() - t0
+    nbytes = int(sl[:take].astype(np.int64).sum()) * k.shape[2] * k.shape[3] * 4
+    return {"value": nbytes * calls / elapsed / 1e12, "unit": "TB/s", "cores": threads, "kind": "port",
+            "sample": f"{take} of {n} sequences x {calls} calls ({elapsed:.1f} s), C oracle "
+                      f"(oracle/pa_oracle.c) on {threads} host threads"}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        barrier = lambda: dist.barrier()  # noqa: E731
+    else:
+        barrier = lambda: None  # noqa: E731
+    assert args.warmup >= 3, "at least 3 warm-up steps"
+    import pad_b200
+    from pad_b200.cases import CONFIGS
+
+    cfg, batch, seq_len, seq_lens = workload_spec(args.workload, world, rank)
+    hq, hkv, d, ps, _ = CONFIGS[cfg]
+    pools, per_step_bytes = make_pools(cfg, batch, seq_len, seq_lens, "cuda", 2.5 * L2_BYTES)
+    npools = len(pools)
+    parts = pad_b200.partitions(local, batch, hkv, hq // hkv, d, ps, pools[0].block_table.shape[1])
+
+    with ClockSampler(local) as clk:
+        ms = time_device(pools, args.steps, args.warmup, torch, barrier)
+    t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = world * per_step_bytes * args.steps / (ms * 1e-3) / 1e12
+    clocks = clk.summary()
+    peak_gbs, peak_kind = peaks()
+    achieved_gbs = per_step_bytes / (ms_per_step * 1e-3) / 1e9
+    traffic = committed_traffic() if cfg == "c2" and batch == 64 else None
+
+    extra = {}
+    if args.no_extras:
+        args.no_sweep = True
+    if rank == 0 and not args.no_extras:
+        e2e_ms, h2d, d2h = time_e2e(pools[0], 10, torch)
+        res_ms, rh2d, rd2h = time_e2e_resident(pools[0], 200, torch)
+        extra["e2e"] = {"value": per_step_bytes / (e2e_ms * 1e-3) / 1e12, "unit": "TB/s",
+                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms}
+        extra["e2e_kv_resident"] = {"value": per_step_bytes / (res_ms * 1e-3) / 1e12, "unit": "TB/s",
+                                    "h2d_bytes_per_step": rh2d, "d2h_bytes_per_step": rd2h,
+                                    "us_per_call": res_ms * 1e3}
+        if world == 1:
+            extra["cpu_baseline"] = cpu_baseline_sample(pools[0])
+    if not args.no_sweep and world == 1 and args.workload == "c2":
+        del pools
+        torch.cuda.empty_cache()
+        sweep = {}
+        for b in (1, 2, 4, 8, 16, 32, 64):
+            pl, nb = make_pools("c2", b, 4096, None, "cuda", 2.5 * L2_BYTES)
+            m = time_device(pl, 1000, 10, torch, barrier) / 1000
+            sweep[str(b)] = {"us_per_call": round(m * 1e3, 3), "TB_s": round(nb / (m * 1e-3) / 1e12, 4),
+                             "frac_of_measured_hbm": round(nb / (m * 1e-3) / 1e9 / peak_gbs, 4)}
+            del pl
+        extra["sweep_c2_seq4096"] = sweep
+        lc = {}
+        for sl_ in (8192, 32768, 131072):
+            pl, nb = make_pools("c3", 1, sl_, None, "cuda", 2.5 * L2_BYTES)
+            m = time_device(pl, 1000, 10, torch, barrier) / 1000
+            lc[str(sl_)] = {"us_per_call": round(m * 1e3, 3), "TB_s": round(nb / (m * 1e-3) / 1e12, 4),
+                            "frac_of_measured_hbm": round(nb / (m * 1e-3) / 1e9 / peak_gbs, 4)}
+            del pl
+        extra["long_context_c3_batch1"] = lc
+
+    if rank == 0:
+        line = {
+            "metric": "decode-attn achieved KV HBM TB/s (Qwen2.5-1.5B shape, seq 4096, batch 64)"
+            if args.workload == "c2" else f"decode-attn achieved KV HBM TB/s ({args.workload})",
+            "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_per_step, "us_per_call": ms_per_step * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16 in / f32 accumulate", "data": "synthetic",
+            "config": {"workload": f"{cfg} batch={batch} per GPU" + (f" seq={seq_len}" if seq_len else ""),
+                       "heads_q_kv": [hq, hkv], "head_dim": d, "page_size": ps, "pages": "random permutation",
+                       "partitions_per_gpu": parts, "l2": f"inputs rotated over {npools} KV pools totalling > 2.5x L2", "parallelism": f"batch-sharded x{world}, no collective"},
+            "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peak_gbs, "unit": "GB/s",
+                         "frac": achieved_gbs / peak_gbs, "traffic": traffic,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                         else "fallback 6650 GB/s",
+                         "kernel_time": "whole step (decode_stream_kernel + merge_kernel) per call"},
+            "clocks": clocks,
+            "gpu_launches": args.steps * (2 if parts > 1 else 1),
+        }
+        line.update(extra)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle
+    from pad_b200.cases import CONFIGS, config_case, kv_bytes
+
+    cfg, batch, seq_len, seq_lens = workload_spec(args.workload, 1, 0)
+    hq, hkv, d, ps, _ = CONFIGS[cfg]
+    c = config_case(cfg, batch=batch, seq_len=seq_len, seq_lens=seq_lens)
+    q, k, v = (a.astype(np.float16) for a in (c.q, c.k_cache, c.v_cache))
+    threads = oracle.max_threads()
+    # bounded sample: as many sequences as keep one step near 1 s
+    t0 = time.perf_counter()
+    oracle.decode_c(q[:1], k, v, c.block_table[:1], c.seq_lens[:1], nthreads=threads)
+    dt = max(time.perf_counter() - t0, 1e-4)
+    take = max(1, min(batch, int(1.0 / dt)))
+    for _ in range(min(args.warmup, 3)):
+        oracle.decode_c(q[:take], k, v, c.block_table[:take], c.seq_lens[:take], nthreads=threads)
+    steps = min(args.steps, 30)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        oracle.decode_c(q[:take], k, v, c.block_table[:take], c.seq_lens[:take], nthreads=threads)
+    el = time.perf_counter() - t0
+    nbytes = kv_bytes(c.seq_lens[:take], hkv, d)
+    value = nbytes * steps / el / 1e12
+    sample = (f"{take} of {batch} sequences per step, {steps} steps; C restatement of src/reference.py "
+              f"(oracle/pa_oracle.c) on {threads} host threads")
+    print(json.dumps({
+        "impl": "reference", "metric": "decode-attn achieved KV HBM TB/s (Qwen2.5-1.5B shape, seq 4096, batch 64)"
+        if args.workload == "c2" else f"decode-attn achieved KV HBM TB/s ({args.workload})",
+        "value": value, "unit": "TB/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": el / steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{cfg} batch={batch}" + (f" seq={seq_len}" if seq_len else ""),
+                   "heads_q_kv": [hq, hkv], "head_dim": d, "page_size": ps},
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -41,58 +41,74 @@ struct Instance {
   const void* kernel;          // decode_stream_kernel<TR>
   const void* merge;           // merge_kernel<D>
   int smem_bytes;
-  int qrows;
   int segw;                    // bytes per row segment (TMA box inner extent)
   bool swz;
+  int hg;                      // KV heads per tile
+  int tt;                      // tokens per tile
 };
 
-template <int D>
-constexpr int stages_for() {
-  return D >= 128 ? 3 : (D == 64 ? 6 : 8);
-}
-
-template <int D, int NT, bool SWZ>
+template <int D, int NT, int HG, bool SWZ>
 Instance make_instance() {
-  using TR = Traits<D, NT, SWZ, stages_for<D>()>;
+  using TR = Traits<D, NT, HG, SWZ>;
   Instance in;
   in.kernel = reinterpret_cast<const void*>(&decode_stream_kernel<TR>);
   in.merge = reinterpret_cast<const void*>(&merge_kernel<D>);
   in.smem_bytes = TR::SMEM_BYTES;
-  in.qrows = TR::QROWS;
   in.segw = TR::SEGW;
   in.swz = SWZ;
+  in.hg = HG;
+  in.tt = TR::TT;
   return in;
 }
 
-template <int D>
-bool pick_nt_swz(int nt, bool swz, Instance* out) {
-  if (nt == 1) *out = swz ? make_instance<D, 1, true>() : make_instance<D, 1, false>();
-  else *out = swz ? make_instance<D, 2, true>() : make_instance<D, 2, false>();
-  return true;
+template <int D, int NT, int HG>
+Instance pick_swz(bool swz) {
+  return swz ? make_instance<D, NT, HG, true>() : make_instance<D, NT, HG, false>();
 }
 
-bool pick_instance(int64_t head_dim, int64_t gqa, bool swz, Instance* out) {
-  const int nt = gqa <= 8 ? 1 : 2;
+template <int D, int NT>
+Instance pick_hg(int hg, bool swz) {
+  switch (hg) {
+    case 8:
+      if constexpr (NT == 1) return pick_swz<D, NT, 8>(swz);
+      else return pick_swz<D, NT, 4>(swz);  // not reached: G > 8 caps the head group at 4
+    case 4: return pick_swz<D, NT, 4>(swz);
+    case 2: return pick_swz<D, NT, 2>(swz);
+    default: return pick_swz<D, NT, 1>(swz);
+  }
+}
+
+// KV heads per tile: the largest of 8, 4, 2, 1 dividing num_kv_heads (at
+// most 4 when a head has more than 8 query rows, to fit shared memory).
+int head_group_for(int64_t hkv, int64_t gqa) {
+  const int cap = gqa <= 8 ? 8 : 4;
+  for (int hg = cap; hg > 1; hg /= 2)
+    if (hkv % hg == 0) return hg;
+  return 1;
+}
+
+bool pick_instance(int64_t head_dim, int64_t gqa, int hg, bool swz, Instance* out) {
+  const bool nt1 = gqa <= 8;
   switch (head_dim) {
-    case 16: return pick_nt_swz<16>(nt, swz, out);
-    case 32: return pick_nt_swz<32>(nt, swz, out);
-    case 64: return pick_nt_swz<64>(nt, swz, out);
-    case 128: return pick_nt_swz<128>(nt, swz, out);
+    case 16: *out = nt1 ? pick_hg<16, 1>(hg, swz) : pick_hg<16, 2>(hg, swz); return true;
+    case 32: *out = nt1 ? pick_hg<32, 1>(hg, swz) : pick_hg<32, 2>(hg, swz); return true;
+    case 64: *out = nt1 ? pick_hg<64, 1>(hg, swz) : pick_hg<64, 2>(hg, swz); return true;
+    case 128: *out = nt1 ? pick_hg<128, 1>(hg, swz) : pick_hg<128, 2>(hg, swz); return true;
     default: return false;
   }
 }
 
-// Largest power of two that divides page_size, capped at one tile: the rows
-// of one TMA box. Boxes never straddle a page or a tile.
-int box_rows_for(int64_t page_size) {
+// Largest power of two that divides page_size, capped at the tile's token
+// count: the token rows of one TMA box. Boxes never straddle a page or a tile.
+int box_rows_for(int64_t page_size, int tt) {
   int r = 1;
-  while (r < kTile && page_size % (2 * r) == 0) r *= 2;
+  while (r < tt && page_size % (2 * r) == 0) r *= 2;
   return r;
 }
 
 // Per-device, per-instance cached facts: opt-in shared memory set, occupancy.
 constexpr int kMaxDevices = 64;
-constexpr int kNumInstanceKeys = 4 * 2 * 2;
+constexpr int kNumInstanceKeys = 4 * 2 * 4 * 2;
 struct DeviceCache {
   int num_sms = 0;
   int occ[kNumInstanceKeys] = {};
@@ -101,9 +117,10 @@ struct DeviceCache {
 DeviceCache g_dev[kMaxDevices];
 std::mutex g_mu;
 
-int instance_key(int64_t head_dim, int64_t gqa, bool swz) {
+int instance_key(int64_t head_dim, int64_t gqa, int hg, bool swz) {
   const int di = head_dim == 16 ? 0 : head_dim == 32 ? 1 : head_dim == 64 ? 2 : 3;
-  return (di * 2 + (gqa <= 8 ? 0 : 1)) * 2 + (swz ? 1 : 0);
+  const int hi = hg == 1 ? 0 : hg == 2 ? 1 : hg == 4 ? 2 : 3;
+  return ((di * 2 + (gqa <= 8 ? 0 : 1)) * 4 + hi) * 2 + (swz ? 1 : 0);
 }
 
 int prepare_device(int device, const Instance& in, int key, int* num_sms, int* occ) {
@@ -157,15 +174,18 @@ int make_plan(int device, int64_t batch, int64_t hkv, int64_t gqa, int64_t head_
     return fail(PAD_ERR_UNSUPPORTED, "head_dim %lld not supported (16, 32, 64 or 128)", (long long)head_dim);
   if (gqa > 16) return fail(PAD_ERR_UNSUPPORTED, "gqa_ratio %lld > 16 not supported", (long long)gqa);
   const int64_t cap = max_pages * page_size;
-  const int64_t tiles_max = (cap + kTile - 1) / kTile;
-  const int64_t tiles_ub = batch * hkv * tiles_max;
-  if (cap > INT32_MAX || tiles_ub > INT32_MAX / 2)
+  const int hg = head_group_for(hkv, gqa);
+  const int tt = kTileRows / hg;
+  const int64_t tiles_max = (cap + tt - 1) / tt;
+  const int64_t groups = hkv / hg;
+  const int64_t tiles_ub = batch * groups * tiles_max;
+  if (cap > INT32_MAX || tiles_ub > INT32_MAX / 2 || batch * groups > INT32_MAX / 4)
     return fail(PAD_ERR_UNSUPPORTED, "problem too large for 32-bit tile indexing (%lld tiles)", (long long)tiles_ub);
-  plan->box_rows = box_rows_for(page_size);
+  plan->box_rows = box_rows_for(page_size, tt);
   const bool swz = plan->box_rows >= 8;
-  if (!pick_instance(head_dim, gqa, swz, &plan->inst))
+  if (!pick_instance(head_dim, gqa, hg, swz, &plan->inst))
     return fail(PAD_ERR_UNSUPPORTED, "no kernel instance for head_dim %lld", (long long)head_dim);
-  plan->key = instance_key(head_dim, gqa, swz);
+  plan->key = instance_key(head_dim, gqa, hg, swz);
   int sms = 0, occ = 0;
   int st = prepare_device(device, plan->inst, plan->key, &sms, &occ);
   if (st != PAD_OK) return st;
@@ -174,16 +194,16 @@ int make_plan(int device, int64_t batch, int64_t hkv, int64_t gqa, int64_t head_
     parts = (int64_t)sms * occ;
     if (parts > tiles_ub) parts = tiles_ub;
   } else {
-    parts = num_splits * batch * hkv;
+    parts = num_splits * batch * groups;
     if (parts > (int64_t)1 << 30) return fail(PAD_ERR_UNSUPPORTED, "num_splits %lld too large", (long long)num_splits);
   }
   if (parts < 1) parts = 1;
   plan->partitions = parts;
-  plan->slots = parts + batch * hkv;
+  plan->slots = parts + batch * groups;
   plan->off_meta = 0;
   plan->off_ml = align_up((size_t)parts * sizeof(int4), 256);
-  plan->off_o = align_up(plan->off_ml + (size_t)plan->slots * gqa * sizeof(float2), 256);
-  plan->bytes = align_up(plan->off_o + (size_t)plan->slots * gqa * head_dim * sizeof(float), 256);
+  plan->off_o = align_up(plan->off_ml + (size_t)plan->slots * hg * gqa * sizeof(float2), 256);
+  plan->bytes = align_up(plan->off_o + (size_t)plan->slots * hg * gqa * head_dim * sizeof(float), 256);
   return PAD_OK;
 }
 
@@ -244,10 +264,10 @@ int pad_version(void) { return 100; }
 int pad_device_info(int device, int64_t head_dim, int64_t gqa_ratio, int* num_sms, int* ctas_per_sm) {
   if (num_sms == nullptr || ctas_per_sm == nullptr) return fail(PAD_ERR_INVALID_ARGUMENT, "null output pointer");
   Instance in;
-  if (gqa_ratio < 1 || gqa_ratio > 16 || !pick_instance(head_dim, gqa_ratio, true, &in))
+  if (gqa_ratio < 1 || gqa_ratio > 16 || !pick_instance(head_dim, gqa_ratio, 1, true, &in))
     return fail(PAD_ERR_UNSUPPORTED, "no kernel for head_dim %lld gqa %lld", (long long)head_dim,
                 (long long)gqa_ratio);
-  return prepare_device(device, in, instance_key(head_dim, gqa_ratio, true), num_sms, ctas_per_sm);
+  return prepare_device(device, in, instance_key(head_dim, gqa_ratio, 1, true), num_sms, ctas_per_sm);
 }
 
 int pad_decode_partitions(int device, int64_t batch, int64_t num_kv_heads, int64_t gqa_ratio, int64_t head_dim,
@@ -331,19 +351,21 @@ int pad_paged_attention_decode(const void* q, const void* k_cache, const void* v
   const Instance& in = plan.inst;
   const CUtensorMapSwizzle swz = swizzle_mode(in);
   {
-    const cuuint64_t dims[4] = {(cuuint64_t)head_dim, (cuuint64_t)num_kv_heads, (cuuint64_t)page_size,
+    // dims ordered {D, token row, KV head, page} so that one box of R tokens x
+    // HG heads lands head-major in shared memory
+    const cuuint64_t dims[4] = {(cuuint64_t)head_dim, (cuuint64_t)page_size, (cuuint64_t)num_kv_heads,
                                 (cuuint64_t)num_pages};
-    const cuuint32_t box[4] = {(cuuint32_t)(in.segw / 2), 1u, (cuuint32_t)plan.box_rows, 1u};
-    const cuuint64_t ks[3] = {(cuuint64_t)k_strides[2] * 2, (cuuint64_t)k_strides[1] * 2,
+    const cuuint32_t box[4] = {(cuuint32_t)(in.segw / 2), (cuuint32_t)plan.box_rows, (cuuint32_t)in.hg, 1u};
+    const cuuint64_t ks[3] = {(cuuint64_t)k_strides[1] * 2, (cuuint64_t)k_strides[2] * 2,
                               (cuuint64_t)k_strides[0] * 2};
-    const cuuint64_t vs[3] = {(cuuint64_t)v_strides[2] * 2, (cuuint64_t)v_strides[1] * 2,
+    const cuuint64_t vs[3] = {(cuuint64_t)v_strides[1] * 2, (cuuint64_t)v_strides[2] * 2,
                               (cuuint64_t)v_strides[0] * 2};
     if ((st = encode_map(&prm.tm_k, k_cache, 4, dims, ks, box, swz, "k_cache")) != PAD_OK) return st;
     if ((st = encode_map(&prm.tm_v, v_cache, 4, dims, vs, box, swz, "v_cache")) != PAD_OK) return st;
   }
   {
     const cuuint64_t dims[3] = {(cuuint64_t)head_dim, (cuuint64_t)num_q_heads, (cuuint64_t)batch};
-    const cuuint32_t box[3] = {(cuuint32_t)(in.segw / 2), (cuuint32_t)gqa, 1u};
+    const cuuint32_t box[3] = {(cuuint32_t)(in.segw / 2), (cuuint32_t)(gqa * in.hg), 1u};
     const cuuint64_t qs[2] = {(cuuint64_t)q_strides[1] * 2, (cuuint64_t)q_strides[0] * 2};
     if ((st = encode_map(&prm.tm_q, q, 3, dims, qs, box, swz, "q")) != PAD_OK) return st;
   }
@@ -376,8 +398,9 @@ int pad_paged_attention_decode(const void* q, const void* k_cache, const void* v
     const float2* a1 = prm.ws_ml;
     const int4* a2 = prm.ws_meta;
     __half* a3 = prm.out;
-    void* margs[] = {&a0, &a1, &a2, &a3, &prm.out_sb, &prm.out_sh, &prm.hkv, &prm.gqa};
-    e = cudaLaunchKernel(in.merge, dim3((unsigned)plan.partitions, (unsigned)gqa), dim3(256), margs, 0, s);
+    int ngroups = (int)(num_kv_heads / in.hg), rows = (int)(gqa * in.hg);
+    void* margs[] = {&a0, &a1, &a2, &a3, &prm.out_sb, &prm.out_sh, &ngroups, &rows};
+    e = cudaLaunchKernel(in.merge, dim3((unsigned)plan.partitions, (unsigned)rows), dim3(256), margs, 0, s);
     if (e != cudaSuccess) return cuda_fail(e, "launching the merge kernel");
   }
   return PAD_OK;

@@ -1,23 +1,26 @@
-// pad_decode_kernel.cuh -- sm_100a paged-attention decode kernels.
+// pad_decode_kernel.cuh -- shared definitions of the sm_100a paged-attention
+// decode kernels (pad_decode_kernels.cuh holds the kernels themselves).
 //
 // Phase 1 (`decode_stream_kernel`): a persistent, stream-K balanced kernel.
-//   The batch is flattened into one list of 64-token tiles ordered
-//   (sequence, KV head, tile); every CTA takes an equal contiguous range of
-//   that list, so work is balanced to within one tile whatever the mix of
-//   sequence lengths. Inside a CTA one producer warp walks its range and
-//   gathers each tile's K/V pages from the paged cache with TMA tensor loads
-//   (block_table gives the page, the tensor map does the addressing) into a
-//   STAGES-deep shared-memory ring guarded by mbarriers; four consumer warps
-//   each take 16 tokens of a tile and run all GQA query rows of the KV head
-//   together on m16n8k16 tensor-core tiles (S^T = K.Q^T, then O^T += V^T.P^T),
-//   with an fp32 online softmax in base 2. When a (sequence, KV head) pair
-//   lies entirely inside one CTA's range the CTA writes the fp16 output row
-//   directly; otherwise it writes an fp32 partial (O, m, l) -- the split-K
-//   partials of the reference's phase 1 (cuda/kernel_v4_split_k.cu:48-150,
-//   analysis/split_k_derivation.md:16-35).
-// Phase 2 (`merge_kernel`): for the pairs that were split across CTAs, a
-//   log-sum-exp merge of the partials (analysis/split_k_derivation.md:44-86),
-//   parallel over (pair, query row) and over the partials themselves.
+//   Work unit: a tile of 128 (token, KV head) rows -- TT tokens of a group of
+//   HG KV heads of one sequence (HG = 8, 4, 2 or 1 heads, TT = 128 / HG). The
+//   batch is flattened into one list of tiles ordered (sequence, head group,
+//   tile) and every CTA takes an equal contiguous range of that list, so work
+//   is balanced to within one tile whatever the mix of sequence lengths.
+//   One producer warp gathers each tile's K/V rows from the paged cache with
+//   TMA tensor loads (block_table names the page; one box spans all HG heads
+//   of R consecutive tokens, i.e. whole contiguous cache rows) into a
+//   STAGES-deep shared-memory ring guarded by mbarriers. Eight consumer
+//   warps each own 16 tokens of one head of the tile and run all GQA query
+//   rows of that head together on m16n8k16 tensor-core tiles
+//   (S^T = K.Q^T, then O^T += V^T.P^T) with an fp32 online softmax in base 2.
+//   A (sequence, head group) pair that lies entirely inside one CTA's range is
+//   finished there (fp16 output); otherwise the CTA writes an fp32 partial
+//   (O, m, l) per head -- the split-K partials of the reference's phase 1
+//   (cuda/kernel_v4_split_k.cu:48-150, analysis/split_k_derivation.md:16-35).
+// Phase 2 (`merge_kernel`): for pairs split across CTAs, a log-sum-exp merge
+//   of the partials (analysis/split_k_derivation.md:44-86), parallel over
+//   (pair, head, query row) and over the partials themselves.
 #pragma once
 
 #include <cuda.h>
@@ -28,77 +31,92 @@
 
 namespace pad {
 
-constexpr int kTile = 64;           // tokens per pipeline tile
-constexpr int kConsumerWarps = 4;   // each owns 16 tokens of a tile
+constexpr int kTileRows = 128;      // (token, head) rows per tile
+constexpr int kConsumerWarps = 8;   // each owns 16 tokens of one head
 constexpr int kThreads = 32 * (kConsumerWarps + 1);
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s: no legitimate wait comes close
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kSmemBudget = 227 * 1024;
 
 struct __align__(64) DecodeParams {
-  CUtensorMap tm_k;  // [D, Hkv, page_size, num_pages] fp16, box {SEG, 1, R, 1}
+  CUtensorMap tm_k;  // dims {D, page_size, Hkv, num_pages}, box {SEG, R, HG, 1}
   CUtensorMap tm_v;
-  CUtensorMap tm_q;  // [D, Hq, B] fp16, box {SEG, G, 1}
+  CUtensorMap tm_q;  // dims {D, Hq, B}, box {SEG, HG*G, 1}
   const int32_t* block_table;
   const int32_t* seq_lens;
   __half* out;
-  float* ws_o;      // [slots][G][D] fp32 unnormalised partial outputs
-  float2* ws_ml;    // [slots][G] (m, l), m in log2 units
+  float* ws_o;      // [slots][HG][G][D] fp32 unnormalised partial outputs
+  float2* ws_ml;    // [slots][HG][G] (m, l), m in log2 units
   int4* ws_meta;    // [partitions] merge descriptors {pair, first slot, n slots, valid}
   int32_t* error_flags;
   int64_t bt_stride;
   int64_t out_sb, out_sh;
   int batch, hkv, gqa, page_size, num_pages, max_pages;
-  int box_rows;      // R: tokens per TMA box (divides page_size and kTile)
+  int box_rows;      // R: tokens per TMA box (divides page_size and TT)
   float scale_log2;  // scale * log2(e)
 };
 
 // Compile-time shape of one kernel instance.
-template <int D_, int NT_, bool SWZ_, int STAGES_>
+template <int D_, int NT_, int HG_, bool SWZ_>
 struct Traits {
   static constexpr int D = D_;
   static constexpr int NT = NT_;            // n8 tiles of query rows: G <= 8*NT
+  static constexpr int HG = HG_;            // KV heads per tile
   static constexpr bool SWZ = SWZ_;         // 128/64/32-byte TMA swizzle (needs R >= 8)
-  static constexpr int STAGES = STAGES_;
-  static constexpr int QROWS = 8 * NT;
+  static constexpr int WPH = kConsumerWarps / HG;  // consumer warps per head
+  static constexpr int TT = 16 * WPH;       // tokens per tile
+  static constexpr int KSTEPS = D / 16;
   static constexpr int ROW_BYTES = D * 2;
   static constexpr int SEGW = SWZ ? (ROW_BYTES < 128 ? ROW_BYTES : 128) : ROW_BYTES;  // bytes per row segment
   static constexpr int NSEG = ROW_BYTES / SEGW;
   static constexpr int CPS = SEGW / 16;     // 16-byte chunks per row segment
-  // Unswizzled tiles place each TMA box (R rows) at a multiple of 128 bytes
-  // (the alignment a tensor copy's shared destination needs), so rows of
-  // fewer than 128 bytes with R * ROW_BYTES < 128 leave gaps between boxes.
-  static constexpr int KT_BYTES = kTile * (SWZ ? ROW_BYTES : (ROW_BYTES < 128 ? 128 : ROW_BYTES));
-  static constexpr int Q_BYTES = QROWS * ROW_BYTES;
-  static constexpr int STAGE_BYTES = ((2 * KT_BYTES + Q_BYTES) + 1023) / 1024 * 1024;
-  static constexpr int NB_MAX = SWZ ? kTile / 8 : kTile;  // TMA boxes per tile (R >= 8 when swizzled)
-  static constexpr int EPI_BYTES = 2 * QROWS * D * 4;
-  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + EPI_BYTES + 4096 /*misc*/;
+  // Unswizzled tiles place each TMA box (HG*R rows) at a multiple of 128
+  // bytes, the alignment a tensor copy's shared destination needs.
+  static constexpr int KT_BYTES = SWZ ? kTileRows * ROW_BYTES
+                                      : TT * (HG * ROW_BYTES < 128 ? 128 : HG * ROW_BYTES);
+  static constexpr int STAGE_BYTES = (2 * KT_BYTES + 1023) / 1024 * 1024;
+  static constexpr int QROWS = HG * 8 * NT;  // query rows held (heads' rows packed, tail zero)
+  static constexpr int Q_BYTES = (QROWS * ROW_BYTES + 1023) / 1024 * 1024;
+  static constexpr int NB_MAX = SWZ ? TT / 8 : TT;  // TMA boxes per tile
+  static constexpr int NB_PER_LANE = (NB_MAX + 31) / 32;
+  // Cross-warp merge buffer (only when several warps share a head).
+  static constexpr int EPI_BYTES = WPH > 1 ? HG * 8 * NT * D * 4 : 0;
+  static constexpr int MISC_BYTES = 4096;
+  // Query tiles in flight: two (one segment ahead) unless that costs a stage.
+  static constexpr int QSLOTS = (kSmemBudget - (1024 + 2 * Q_BYTES + EPI_BYTES + MISC_BYTES)) / STAGE_BYTES >= 3 ? 2 : 1;
+  static constexpr int FIXED_BYTES = 1024 /*align slack*/ + QSLOTS * Q_BYTES + EPI_BYTES + MISC_BYTES;
+  static constexpr int STAGES_FIT = (kSmemBudget - FIXED_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 4 ? 4 : STAGES_FIT;
+  static_assert(STAGES >= 2, "tile ring does not fit in shared memory");
+  static constexpr int SMEM_BYTES = FIXED_BYTES + STAGES * STAGE_BYTES;
 
   // XOR applied to the 16-byte chunk index of a row by the TMA swizzle mode
-  // (the chunk bits [4,4+b) of the shared address are XOR-ed with bits [7,7+b)).
+  // (chunk bits [4,4+b) of the shared address XOR-ed with bits [7,7+b)).
   __device__ static __forceinline__ uint32_t swz(uint32_t row) {
     if constexpr (!SWZ) return 0u;
     else if constexpr (SEGW == 128) return row & 7u;
     else if constexpr (SEGW == 64) return (row >> 1) & 3u;
     else return (row >> 2) & 1u;
   }
-  // Bytes between consecutive TMA boxes of R rows in a K/V tile.
+  // Bytes between consecutive TMA boxes (HG heads x R tokens) of a tile segment.
   __device__ static __forceinline__ uint32_t box_pitch(int R) {
-    if constexpr (SWZ) return (uint32_t)(R * SEGW);
-    else return (uint32_t)(R * ROW_BYTES < 128 ? 128 : R * ROW_BYTES);
+    if constexpr (SWZ) return (uint32_t)(HG * R * SEGW);
+    else return (uint32_t)(HG * R * ROW_BYTES < 128 ? 128 : HG * R * ROW_BYTES);
   }
-  // Shared address of 16-byte chunk `c` (0 .. D/8-1) of token row `row` of a
-  // K/V tile stored from `base` (segment-major when swizzled; box-pitched
-  // when not). R = rows per TMA box.
-  __device__ static __forceinline__ uint32_t kv_addr(uint32_t base, uint32_t row, uint32_t c, int R) {
+  // Shared address of 16-byte chunk `c` (0 .. D/8-1) of token `t` (0 .. TT-1),
+  // local head `hl` of a K/V tile at `base`. A box j holds tokens
+  // [j*R, j*R + R) of all HG heads, head-major ([hl][r]).
+  __device__ static __forceinline__ uint32_t kv_addr(uint32_t base, uint32_t t, uint32_t hl, uint32_t c, int R) {
+    const uint32_t j = t / R, r = t % R;
     if constexpr (SWZ) {
+      const uint32_t idx = (j * HG + hl) * R + r;
       const uint32_t seg = c / CPS, cs = c % CPS;
-      return base + seg * (uint32_t)(kTile * SEGW) + row * SEGW + ((cs ^ swz(row)) << 4);
+      return base + seg * (uint32_t)(kTileRows * SEGW) + idx * SEGW + ((cs ^ swz(idx)) << 4);
     } else {
-      return base + (row / R) * box_pitch(R) + (row % R) * ROW_BYTES + (c << 4);
+      return base + j * box_pitch(R) + (hl * R + r) * ROW_BYTES + (c << 4);
     }
   }
-  // Same for the query tile (one box of QROWS rows).
+  // Query tile: HG*G rows packed (head hl at rows hl*G ..), segment-major.
   __device__ static __forceinline__ uint32_t q_addr(uint32_t base, uint32_t row, uint32_t c) {
     const uint32_t seg = c / CPS, cs = c % CPS;
     return base + seg * (uint32_t)(QROWS * SEGW) + row * SEGW + ((cs ^ swz(row)) << 4);
@@ -107,20 +125,20 @@ struct Traits {
 
 // Shared-memory bookkeeping beside the stage ring.
 struct TileDesc {
-  int b, h, i, seq;   // sequence, KV head, tile index within the pair, clamped seq_len
+  int b, hg, i, seq;  // sequence, head group, tile index within the pair, clamped seq_len
   int flags;          // kFirst | kLast | kSplit
   int slot;           // partial slot when split
-  int pad0, pad1;
+  int qslot;          // query-tile ring slot of this segment
+  int pad;
 };
 constexpr int kFirst = 1, kLast = 2, kSplit = 4;
 
 struct Cursor {
-  int b, h, i, n, seq;  // n = tiles of sequence b
-  int pair_start;       // global index of tile 0 of pair (b, h)
+  int b, hg, i, n, seq;  // n = tiles of sequence b
+  int pair_start;        // global index of tile 0 of pair (b, hg)
 };
 
 __device__ __forceinline__ int clamp_seq(int raw, int cap) { return raw < 0 ? 0 : (raw > cap ? cap : raw); }
-__device__ __forceinline__ int tiles_of(int seq) { return (seq + kTile - 1) / kTile; }
 
 // Partition w of W covers global tiles [begin(w), begin(w+1)).
 __device__ __forceinline__ int part_begin(int64_t w, int64_t total, int64_t parts) {
@@ -129,23 +147,6 @@ __device__ __forceinline__ int part_begin(int64_t w, int64_t total, int64_t part
 // The partition owning global tile t: the largest w with begin(w) <= t.
 __device__ __forceinline__ int part_owner(int64_t t, int64_t total, int64_t parts) {
   return (int)(((t + 1) * parts - 1) / total);
-}
-
-// Step a cursor to the next tile of the flattened (sequence, head, tile) list.
-__device__ __forceinline__ void cursor_next(Cursor& c, const DecodeParams& p, int cap) {
-  if (++c.i < c.n) return;
-  c.i = 0;
-  c.pair_start += c.n;
-  if (++c.h < p.hkv) return;
-  c.h = 0;
-  do {
-    if (++c.b >= p.batch) {
-      c.n = 0;
-      return;
-    }
-    c.seq = clamp_seq(__ldg(p.seq_lens + c.b), cap);
-    c.n = tiles_of(c.seq);
-  } while (c.n == 0);
 }
 
 }  // namespace pad

@@ -11,27 +11,55 @@ __device__ __forceinline__ void raise_flag(const DecodeParams& p, int bits) {
   if (p.error_flags != nullptr) atomicOr(p.error_flags, bits);
 }
 
-// Page ids of the TMA boxes of the tile at cursor `c`: lane j loads box j (and
-// j + 32 when a tile has more than 32 boxes). Boxes past seq_len get id 0 and
-// are never issued.
 template <class TR>
-__device__ __forceinline__ void load_page_ids(const DecodeParams& p, const Cursor& c, int lane, int (&dst)[2]) {
+__device__ __forceinline__ int tiles_of(int seq) {
+  return (seq + TR::TT - 1) / TR::TT;
+}
+
+// Step a cursor to the next tile of the flattened (sequence, head group,
+// tile) list; past the end it reports n = 0.
+template <class TR>
+__device__ __forceinline__ void cursor_next(Cursor& c, const DecodeParams& p, int cap, int ngroups) {
+  if (++c.i < c.n) return;
+  c.i = 0;
+  c.pair_start += c.n;
+  if (++c.hg < ngroups) return;
+  c.hg = 0;
+  do {
+    if (++c.b >= p.batch) {
+      c.n = 0;
+      return;
+    }
+    c.seq = clamp_seq(__ldg(p.seq_lens + c.b), cap);
+    c.n = tiles_of<TR>(c.seq);
+  } while (c.n == 0);
+}
+
+// Page ids of the TMA boxes of the tile at cursor `c`: lane l loads boxes
+// l, l + 32, ... Boxes past seq_len get id 0 and are never issued.
+template <class TR>
+__device__ __forceinline__ void load_page_ids(const DecodeParams& p, const Cursor& c, int lane,
+                                              int (&dst)[TR::NB_PER_LANE]) {
   const int R = p.box_rows;
   const int64_t row = (int64_t)c.b * p.bt_stride;
 #pragma unroll
-  for (int u = 0; u < 2; ++u) {
+  for (int u = 0; u < TR::NB_PER_LANE; ++u) {
     const int j = lane + 32 * u;
-    dst[u] = 0;
-    if (TR::NB_MAX > 32 || u == 0) {
-      const int tok = c.i * kTile + j * R;
-      if (j * R < kTile && tok < c.seq) dst[u] = __ldg(p.block_table + row + tok / p.page_size);
-    }
+    const int tok = c.i * TR::TT + j * R;
+    dst[u] = (j * R < TR::TT && tok < c.seq) ? __ldg(p.block_table + row + tok / p.page_size) : 0;
   }
 }
 
-// Cross-warp epilogue sync on an mbarrier (count = consumer warps) with a
-// bounded wait. Returns false on timeout.
-__device__ __forceinline__ bool epi_sync(uint64_t* bar, uint32_t& phase, int lane) {
+template <class TR>
+__device__ __forceinline__ void store_page_ids(int* slot_ids, int lane, const int (&v)[TR::NB_PER_LANE]) {
+#pragma unroll
+  for (int u = 0; u < TR::NB_PER_LANE; ++u)
+    if (lane + 32 * u < TR::NB_MAX) slot_ids[lane + 32 * u] = v[u];
+}
+
+// Cross-warp sync of the consumer warps on an mbarrier (count = consumer
+// warps) with a bounded wait. Returns false on timeout.
+__device__ __forceinline__ bool consumer_sync(uint64_t* bar, uint32_t& phase, int lane) {
   __syncwarp();
   if (lane == 0) mbar_arrive(bar);
   const bool ok = mbar_wait_bounded(bar, phase, kWaitTimeoutNs);
@@ -42,37 +70,45 @@ __device__ __forceinline__ bool epi_sync(uint64_t* bar, uint32_t& phase, int lan
 
 template <class TR>
 __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid_constant__ DecodeParams p) {
-  constexpr int D = TR::D, NT = TR::NT, S = TR::STAGES, QROWS = TR::QROWS, KSTEPS = D / 16;
+  constexpr int D = TR::D, NT = TR::NT, HG = TR::HG, S = TR::STAGES, KSTEPS = TR::KSTEPS;
+  constexpr int TT = TR::TT, WPH = TR::WPH;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
-  float* epi = reinterpret_cast<float*>(smem + S * TR::STAGE_BYTES);  // [2][QROWS][D]
-  uint64_t* full = reinterpret_cast<uint64_t*>(epi + 2 * QROWS * D);
+  uint8_t* qtiles = smem + S * TR::STAGE_BYTES;                        // [TR::QSLOTS][Q_BYTES]
+  float* epi = reinterpret_cast<float*>(qtiles + TR::QSLOTS * TR::Q_BYTES);  // [HG][8*NT][D]
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(epi) + TR::EPI_BYTES);
   uint64_t* empty = full + S;
-  uint64_t* ebar = empty + S;
+  uint64_t* qfull = empty + S;
+  uint64_t* qempty = qfull + TR::QSLOTS;
+  uint64_t* ebar = qempty + TR::QSLOTS;
   TileDesc* descs = reinterpret_cast<TileDesc*>(ebar + 2);
-  int* ids = reinterpret_cast<int*>(descs + S);             // [S][NB_MAX]
-  float2* sml = reinterpret_cast<float2*>(ids + S * TR::NB_MAX);  // [warps][QROWS]
-  float2* sML = sml + kConsumerWarps * QROWS;                   // [QROWS]
-  int* scan = reinterpret_cast<int*>(sML + QROWS);              // [8]
-  volatile int* abort_flag = scan + 8;
-  int* cur_smem = scan + 12;                                    // Cursor as 6 ints
+  int* ids = reinterpret_cast<int*>(descs + S);                      // [S][NB_MAX]
+  float2* sml = reinterpret_cast<float2*>(ids + S * TR::NB_MAX);     // [warps][8*NT]
+  float2* sML = sml + kConsumerWarps * 8 * NT;                       // [HG][8*NT]
+  int* scan = reinterpret_cast<int*>(sML + HG * 8 * NT);             // [kThreads/32]
+  volatile int* abort_flag = scan + 12;
+  int* cur_smem = scan + 16;                                         // Cursor as 6 ints
+  int* sink = scan + 24;                                             // [consumer warps] scratch
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int cap = p.max_pages * p.page_size;
   const int64_t W = gridDim.x;
   const int w = blockIdx.x;
   const int G = p.gqa;
+  const int ngroups = p.hkv / HG;
 
-  // ---- set-up: zero the Q tiles (rows >= G stay zero), init barriers
-  for (int s = 0; s < S; ++s) {
-    uint4* qz = reinterpret_cast<uint4*>(stages + s * TR::STAGE_BYTES + 2 * TR::KT_BYTES);
-    for (int x = tid; x < TR::Q_BYTES / 16; x += kThreads) qz[x] = make_uint4(0, 0, 0, 0);
-  }
+  // ---- set-up: zero the query tiles (rows past HG*G stay zero), init barriers
+  for (int x = tid; x < TR::QSLOTS * TR::Q_BYTES / 16; x += kThreads)
+    reinterpret_cast<uint4*>(qtiles)[x] = make_uint4(0, 0, 0, 0);
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
+    }
+    for (int s = 0; s < TR::QSLOTS; ++s) {
+      mbar_init(&qfull[s], 1);
+      mbar_init(&qempty[s], kConsumerWarps);
     }
     mbar_init(&ebar[0], kConsumerWarps);
     *abort_flag = 0;
@@ -80,16 +116,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     fence_mbar_init();
   }
 
-  // ---- block-wide exclusive scan of tiles per sequence (x Hkv)
+  // ---- block-wide exclusive scan of tiles per sequence (x head groups)
   const int per = (p.batch + kThreads - 1) / kThreads;
   const int b_lo = min(p.batch, tid * per), b_hi = min(p.batch, b_lo + per);
   int local = 0, bad = 0;
   for (int b = b_lo; b < b_hi; ++b) {
     const int raw = __ldg(p.seq_lens + b);
     bad |= (raw < 0 || raw > cap);
-    local += tiles_of(clamp_seq(raw, cap));
+    local += tiles_of<TR>(clamp_seq(raw, cap));
   }
-  local *= p.hkv;
+  local *= ngroups;
   int incl = local;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -104,15 +140,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     if (x < warp) excl += v;
     total += v;
   }
-  if (bad && w == 0 && p.error_flags != nullptr) atomicOr(p.error_flags, PAD_FLAG_SEQ_LEN_RANGE);
+  if (bad && w == 0) raise_flag(p, PAD_FLAG_SEQ_LEN_RANGE);
   const int t0 = total > 0 ? part_begin(w, total, W) : 0;
   const int t1 = total > 0 ? part_begin(w + 1, total, W) : 0;
   if (t0 < total && excl <= t0 && t0 < excl + local) {
     int acc_t = excl;
     for (int b = b_lo; b < b_hi; ++b) {
       const int seq = clamp_seq(__ldg(p.seq_lens + b), cap);
-      const int n = tiles_of(seq);
-      const int tb = n * p.hkv;
+      const int n = tiles_of<TR>(seq);
+      const int tb = n * ngroups;
       if (t0 < acc_t + tb) {
         const int o = t0 - acc_t;
         cur_smem[0] = b;
@@ -126,7 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
       acc_t += tb;
     }
   }
-  fence_proxy_async_smem();  // zeroed Q tiles before any TMA write into the stages
+  fence_proxy_async_smem();  // zeroed query tiles before any TMA write to them
   __syncthreads();
 
   // ---- zero output rows of empty sequences (src/reference.py:32-34)
@@ -148,77 +184,84 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     if (ntiles <= 0) {
       // An empty partition (more partitions than tiles) can sit between the
       // first and last partition of a split pair; it owns a partial slot of
-      // that pair, which it marks empty (m = -inf, l = 0).
+      // that pair, which it marks empty (m = -inf, l = 0) for every head.
       if (cur_smem[0] >= 0 && cur_smem[5] < t0) {
-        const int slot = cur_smem[0] * p.hkv + cur_smem[1] + w;
-        for (int g = lane; g < G; g += 32) p.ws_ml[(int64_t)slot * G + g] = make_float2(-INFINITY, 0.f);
+        const int slot = cur_smem[0] * ngroups + cur_smem[1] + w;
+        for (int x = lane; x < HG * G; x += 32) p.ws_ml[(int64_t)slot * HG * G + x] = make_float2(-INFINITY, 0.f);
       }
       return;
     }
     const int R = p.box_rows;
     Cursor c{cur_smem[0], cur_smem[1], cur_smem[2], cur_smem[3], cur_smem[4], cur_smem[5]};
     Cursor la = c;
-    int pid[S][2];
+    int pid[S][TR::NB_PER_LANE];
 #pragma unroll
     for (int k = 0; k < S; ++k) {
-      pid[k][0] = pid[k][1] = 0;
       if (k < ntiles) {
         load_page_ids<TR>(p, la, lane, pid[k]);
-        cursor_next(la, p, cap);
+        cursor_next<TR>(la, p, cap, ngroups);
       }
     }
 #pragma unroll
-    for (int k = 0; k < S; ++k) {
-      if (lane < TR::NB_MAX) ids[k * TR::NB_MAX + lane] = pid[k][0];
-      if constexpr (TR::NB_MAX > 32) ids[k * TR::NB_MAX + 32 + lane] = pid[k][1];
-    }
+    for (int k = 0; k < S; ++k)
+      if (k < ntiles) store_page_ids<TR>(ids + k * TR::NB_MAX, lane, pid[k]);
     __syncwarp();
-    int pend[2] = {0, 0};
+    int pend[TR::NB_PER_LANE];
     bool have_pend = false;
-    int issued = 0;
+    int issued = 0, segs = 0;
     bool ok = true;
+    const uint32_t qbytes = (uint32_t)(HG * G * TR::ROW_BYTES);
     for (int k = 0; k < ntiles; ++k) {
       const int s = k % S;
-      if (k >= S) {
-        if (!mbar_wait_bounded(&empty[s], ((k / S) - 1) & 1, kWaitTimeoutNs)) ok = false;
-        if (__any_sync(0xffffffffu, !ok) || *abort_flag) {
-          ok = false;
-          break;
-        }
+      if (k >= S) ok = mbar_wait_bounded(&empty[s], ((k / S) - 1) & 1, kWaitTimeoutNs);
+      if (!__all_sync(0xffffffffu, ok) || *abort_flag) {
+        ok = false;
+        break;
       }
       if (have_pend) {
-        const int ps = (k - 1) % S;
-        if (lane < TR::NB_MAX) ids[ps * TR::NB_MAX + lane] = pend[0];
-        if constexpr (TR::NB_MAX > 32) ids[ps * TR::NB_MAX + 32 + lane] = pend[1];
+        store_page_ids<TR>(ids + ((k - 1) % S) * TR::NB_MAX, lane, pend);
         have_pend = false;
       }
       __syncwarp();
-      const int tok0 = c.i * kTile;
-      const int vt = min(kTile, c.seq - tok0);
+      const int tok0 = c.i * TT;
+      const int vt = min(TT, c.seq - tok0);
       const int nvalid = (vt + R - 1) / R;
       const bool first = (k == 0) || (c.i == 0);
       const bool last = (k == ntiles - 1) || (c.i == c.n - 1);
-      const int pair = c.b * p.hkv + c.h;
+      const int pair = c.b * ngroups + c.hg;
       const bool split = !(c.pair_start >= t0 && c.pair_start + c.n <= t1);
+      const int qs = segs % TR::QSLOTS;
+      if (first) {
+        // the query tile of this segment: wait until its ring slot is free
+        if (segs >= TR::QSLOTS) ok = mbar_wait_bounded(&qempty[qs], ((segs / TR::QSLOTS) - 1) & 1, kWaitTimeoutNs);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&qfull[qs], qbytes);
+#pragma unroll
+          for (int sg = 0; sg < TR::NSEG; ++sg)
+            tma_load_3d(qtiles + qs * TR::Q_BYTES + sg * TR::QROWS * TR::SEGW, &p.tm_q, &qfull[qs],
+                        sg * (TR::SEGW / 2), c.hg * HG * G, c.b);
+        }
+      }
       if (lane == 0) {
         TileDesc dsc;
         dsc.b = c.b;
-        dsc.h = c.h;
+        dsc.hg = c.hg;
         dsc.i = c.i;
         dsc.seq = c.seq;
         dsc.flags = (first ? kFirst : 0) | (last ? kLast : 0) | (split ? kSplit : 0);
         // Partial slots: pair p uses slots [p + owner(start_p), ...], one per
         // partition touching it; partition w writes slot p + w. These ranges
-        // are disjoint across pairs and never exceed partitions + pairs.
+        // are disjoint across pairs and stay below partitions + pairs.
         dsc.slot = pair + w;
-        dsc.pad0 = dsc.pad1 = 0;
+        dsc.qslot = qs;
+        dsc.pad = 0;
         descs[s] = dsc;
-        if (split && c.i == 0 && first) {
+        if (split && c.i == 0) {
           const int last_owner = part_owner((int64_t)c.pair_start + c.n - 1, total, W);
           p.ws_meta[w] = make_int4(pair, pair + w, last_owner - w + 1, 1);
         }
-        const uint32_t bytes = (uint32_t)nvalid * R * TR::ROW_BYTES * 2 + (first ? (uint32_t)G * TR::ROW_BYTES : 0u);
-        mbar_arrive_expect_tx(&full[s], bytes);
+        mbar_arrive_expect_tx(&full[s], (uint32_t)nvalid * R * HG * TR::ROW_BYTES * 2);
       }
       __syncwarp();
       uint8_t* st = stages + s * TR::STAGE_BYTES;
@@ -228,24 +271,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
         const int row = (tok0 + j * R) % p.page_size;
 #pragma unroll
         for (int sg = 0; sg < TR::NSEG; ++sg) {
-          const int off = sg * kTile * TR::SEGW + j * (int)TR::box_pitch(R);
-          tma_load_4d(st + off, &p.tm_k, &full[s], sg * (TR::SEGW / 2), c.h, row, page);
-          tma_load_4d(st + TR::KT_BYTES + off, &p.tm_v, &full[s], sg * (TR::SEGW / 2), c.h, row, page);
+          const int off = sg * kTileRows * TR::SEGW + j * (int)TR::box_pitch(R);
+          tma_load_4d(st + off, &p.tm_k, &full[s], sg * (TR::SEGW / 2), row, c.hg * HG, page);
+          tma_load_4d(st + TR::KT_BYTES + off, &p.tm_v, &full[s], sg * (TR::SEGW / 2), row, c.hg * HG, page);
         }
       }
-      if (first && lane == 0) {
-#pragma unroll
-        for (int sg = 0; sg < TR::NSEG; ++sg)
-          tma_load_3d(st + 2 * TR::KT_BYTES + sg * QROWS * TR::SEGW, &p.tm_q, &full[s], sg * (TR::SEGW / 2), c.h * G,
-                      c.b);
-      }
       ++issued;
+      if (first) ++segs;
       if (k + S < ntiles) {
         load_page_ids<TR>(p, la, lane, pend);
-        cursor_next(la, p, cap);
+        cursor_next<TR>(la, p, cap, ngroups);
         have_pend = true;
       }
-      cursor_next(c, p, cap);
+      cursor_next<TR>(c, p, cap, ngroups);
     }
     if (!ok) {
       // Unwind: record the failure, stop the consumers, and wait (bounded)
@@ -255,6 +293,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
         *abort_flag = 1;
         for (int k = max(0, issued - S); k < issued; ++k)
           (void)mbar_wait_bounded(&full[k % S], (k / S) & 1, kWaitTimeoutNs / 4);
+        if (segs > 0)
+          (void)mbar_wait_bounded(&qfull[(segs - 1) % TR::QSLOTS], ((segs - 1) / TR::QSLOTS) & 1, kWaitTimeoutNs / 4);
       }
     }
     return;
@@ -262,41 +302,49 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
 
   // =============================== consumer warps ===============================
   if (ntiles <= 0) return;
-  const int gl = 2 * (lane & 3);  // first query row (within an n8 tile) this lane owns
+  const int hl = warp / WPH;               // local KV head this warp serves
+  const uint32_t t_base = (warp % WPH) * 16;  // its 16 tokens within the tile
+  const int R = p.box_rows;
+  const int gl = 2 * (lane & 3);            // first query row (within an n8 tile) this lane owns
   uint32_t qf[KSTEPS][NT][2];
   float acc[KSTEPS][NT][4];
   float m_run[NT][2], l_run[NT][2];
   uint32_t ephase = 0;
-  const uint32_t r0 = warp * 16;
+  int segs = 0;
 
   for (int k = 0; k < ntiles; ++k) {
     const int s = k % S;
     bool ok = mbar_wait_bounded(&full[s], (k / S) & 1, kWaitTimeoutNs);
-    if (!__all_sync(0xffffffffu, ok) || *abort_flag) {
-      if (lane == 0) {
-        raise_flag(p, PAD_FLAG_WAIT_TIMEOUT);
-        *abort_flag = 1;
-      }
-      return;
-    }
     const TileDesc dsc = descs[s];
-    const uint32_t kb = smem_u32(stages + s * TR::STAGE_BYTES);
-    const uint32_t vb = kb + TR::KT_BYTES;
-    const uint32_t qb = kb + 2 * TR::KT_BYTES;
-
-    if (dsc.flags & kFirst) {
+    if (ok && (dsc.flags & kFirst)) {
+      const int qs = dsc.qslot;
+      ok = mbar_wait_bounded(&qfull[qs], (segs / TR::QSLOTS) & 1, kWaitTimeoutNs);
+      const uint32_t qb = smem_u32(qtiles + qs * TR::Q_BYTES);
+      const uint32_t qrow0 = hl * G;
       if constexpr (KSTEPS == 1) {
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
-          ldsm_x2(TR::q_addr(qb, nt * 8 + (lane & 7), (lane >> 3) & 1), qf[0][nt][0], qf[0][nt][1]);
+          ldsm_x2(TR::q_addr(qb, qrow0 + nt * 8 + (lane & 7), (lane >> 3) & 1), qf[0][nt][0], qf[0][nt][1]);
       } else {
 #pragma unroll
         for (int kk = 0; kk < KSTEPS; kk += 2)
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt)
-            ldsm_x4(TR::q_addr(qb, nt * 8 + (lane & 7), kk * 2 + (lane >> 3)), qf[kk][nt][0],
+            ldsm_x4(TR::q_addr(qb, qrow0 + nt * 8 + (lane & 7), kk * 2 + (lane >> 3)), qf[kk][nt][0],
                     qf[kk][nt][1], qf[kk + 1][nt][0], qf[kk + 1][nt][1]);
       }
+      // The slot may be refilled by TMA as soon as it is released, so every
+      // lane must have its ldmatrix results in registers first: a store that
+      // depends on all fragment registers makes the warp wait for them.
+      uint32_t chk = 0;
+#pragma unroll
+      for (int kk = 0; kk < KSTEPS; ++kk)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) chk ^= qf[kk][nt][0] ^ qf[kk][nt][1];
+      asm volatile("st.shared.u32 [%0], %1;" ::"r"(smem_u32(sink + warp)), "r"(chk) : "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&qempty[qs]);
+      ++segs;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         m_run[nt][0] = m_run[nt][1] = -INFINITY;
@@ -307,16 +355,25 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
           for (int e = 0; e < 4; ++e) acc[mt][nt][e] = 0.f;
       }
     }
+    if (!__all_sync(0xffffffffu, ok) || *abort_flag) {
+      if (lane == 0) {
+        raise_flag(p, PAD_FLAG_WAIT_TIMEOUT);
+        *abort_flag = 1;
+      }
+      return;
+    }
+    const uint32_t kb = smem_u32(stages + s * TR::STAGE_BYTES);
+    const uint32_t vb = kb + TR::KT_BYTES;
 
-    const int nv = min(16, dsc.seq - (dsc.i * kTile + (int)r0));
+    const int nv = min(16, dsc.seq - (dsc.i * TT + (int)t_base));
     if (nv > 0) {
       if (nv < 16) {
         // Rows past seq_len hold whatever the page (or an earlier tile) left
         // there -- possibly NaN/Inf. Zero this warp's V rows so 0-probability
         // tokens contribute exactly 0; K rows are masked through the scores.
         for (int x = lane; x < (16 - nv) * (D / 8); x += 32) {
-          const uint32_t row = r0 + nv + x / (D / 8), cc = x % (D / 8);
-          asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(TR::kv_addr(vb, row, cc, p.box_rows)), "r"(0)
+          const uint32_t t = t_base + nv + x / (D / 8), cc = x % (D / 8);
+          asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(TR::kv_addr(vb, t, hl, cc, R)), "r"(0)
                        : "memory");
         }
         fence_proxy_async_smem();
@@ -329,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
 #pragma unroll
       for (int kk = 0; kk < KSTEPS; ++kk) {
         uint32_t a0, a1, a2, a3;
-        ldsm_x4(TR::kv_addr(kb, r0 + (lane & 7) + ((lane >> 3) & 1) * 8, kk * 2 + (lane >> 4), p.box_rows), a0, a1,
+        ldsm_x4(TR::kv_addr(kb, t_base + (lane & 7) + ((lane >> 3) & 1) * 8, hl, kk * 2 + (lane >> 4), R), a0, a1,
                 a2, a3);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) mma_16816(sc[nt], a0, a1, a2, a3, qf[kk][nt][0], qf[kk][nt][1]);
@@ -378,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
 #pragma unroll
       for (int mt = 0; mt < KSTEPS; ++mt) {
         uint32_t a0, a1, a2, a3;
-        ldsm_x4_trans(TR::kv_addr(vb, r0 + (lane & 7) + ((lane >> 4) & 1) * 8, mt * 2 + ((lane >> 3) & 1), p.box_rows),
+        ldsm_x4_trans(TR::kv_addr(vb, t_base + (lane & 7) + ((lane >> 4) & 1) * 8, hl, mt * 2 + ((lane >> 3) & 1), R),
                       a0, a1, a2, a3);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) mma_16816(acc[mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
@@ -388,7 +445,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     if (lane == 0) mbar_arrive(&empty[s]);
 
     if (dsc.flags & kLast) {
-      // ---------------- segment epilogue: merge the 4 warps, write out / partial
+      // ------------- segment epilogue: merge the WPH warps of each head, write
+      // the fp16 output rows (pair finished here) or the fp32 partial (split pair)
+      float lsum[NT][2];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -397,104 +456,134 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
           l += __shfl_xor_sync(0xffffffffu, l, 4);
           l += __shfl_xor_sync(0xffffffffu, l, 8);
           l += __shfl_xor_sync(0xffffffffu, l, 16);
-          l_run[nt][j] = l;
-          if ((lane >> 2) == 0) sml[warp * QROWS + nt * 8 + gl + j] = make_float2(m_run[nt][j], l);
+          lsum[nt][j] = l;
         }
-      bool eok = epi_sync(&ebar[0], ephase, lane);
-      float scl[NT][2];
+      const bool split = (dsc.flags & kSplit) != 0;
+      const int qrow0 = dsc.hg * HG * G + hl * G;  // first query head of this warp's KV head
+      if constexpr (WPH == 1) {
+        // one warp per head: write straight from the accumulator fragments
+        const int64_t prow = ((int64_t)dsc.slot * HG + hl) * G;
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
+        for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int g = nt * 8 + gl + j;
-          float M = -INFINITY;
+          for (int j = 0; j < 2; ++j) {
+            const int g = nt * 8 + gl + j;
+            if (g >= G) continue;
+            const float L = lsum[nt][j];
+            const float inv = L > 0.f ? 1.f / L : 0.f;
+            if (split && (lane >> 2) == 0) p.ws_ml[prow + g] = make_float2(m_run[nt][j], L);
 #pragma unroll
-          for (int ww = 0; ww < kConsumerWarps; ++ww) M = fmaxf(M, sml[ww * QROWS + g].x);
-          const float Mu = (M == -INFINITY) ? 0.f : M;
-          float L = 0.f;
+            for (int mt = 0; mt < KSTEPS; ++mt)
 #pragma unroll
-          for (int ww = 0; ww < kConsumerWarps; ++ww) {
-            const float2 x = sml[ww * QROWS + g];
-            L += x.y * ex2(x.x - Mu);
-          }
-          scl[nt][j] = ex2(m_run[nt][j] - Mu);
-          if (warp == 0 && (lane >> 2) == 0) sML[g] = make_float2(Mu, L);
-        }
-      // warps 0,1 store their scaled O^T into two buffers, then warps 2,3 add
-      float* buf = epi + (warp & 1) * QROWS * D;
-#pragma unroll
-      for (int half_pass = 0; half_pass < 2; ++half_pass) {
-        if ((warp >> 1) == half_pass) {
-#pragma unroll
-          for (int mt = 0; mt < KSTEPS; ++mt)
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int d = mt * 16 + (lane >> 2) + (e >= 2 ? 8 : 0);
-                const int g = nt * 8 + gl + (e & 1);
-                const float v = acc[mt][nt][e] * scl[nt][e & 1];
-                if (half_pass == 0) buf[g * D + d] = v;
-                else buf[g * D + d] += v;
+              for (int hi = 0; hi < 2; ++hi) {
+                const int d = mt * 16 + (lane >> 2) + hi * 8;
+                const float v = acc[mt][nt][j + 2 * hi];
+                if (split) p.ws_o[(prow + g) * D + d] = v;
+                else p.out[dsc.b * p.out_sb + (int64_t)(qrow0 + g) * p.out_sh + d] = __float2half_rn(v * inv);
               }
-        }
-        eok &= epi_sync(&ebar[0], ephase, lane);
-      }
-      const int ctid = warp * 32 + lane;
-      if (!(dsc.flags & kSplit)) {
-        __half* orow = p.out + dsc.b * p.out_sb + (int64_t)(dsc.h * G) * p.out_sh;
-        for (int x = ctid; x < G * (D / 2); x += 32 * kConsumerWarps) {
-          const int g = x / (D / 2), d = (x % (D / 2)) * 2;
-          const float L = sML[g].y;
-          const float inv = L > 0.f ? 1.f / L : 0.f;
-          const float v0 = epi[g * D + d] + epi[QROWS * D + g * D + d];
-          const float v1 = epi[g * D + d + 1] + epi[QROWS * D + g * D + d + 1];
-          *reinterpret_cast<__half2*>(orow + g * p.out_sh + d) = __floats2half2_rn(v0 * inv, v1 * inv);
-        }
+          }
       } else {
-        float4* o4 = reinterpret_cast<float4*>(p.ws_o + (int64_t)dsc.slot * G * D);
-        for (int x = ctid; x < G * (D / 4); x += 32 * kConsumerWarps) {
-          const int g = x / (D / 4), d = (x % (D / 4)) * 4;
-          const float4 a = *reinterpret_cast<const float4*>(epi + g * D + d);
-          const float4 bq = *reinterpret_cast<const float4*>(epi + QROWS * D + g * D + d);
-          o4[x] = make_float4(a.x + bq.x, a.y + bq.y, a.z + bq.z, a.w + bq.w);
+        if ((lane >> 2) == 0) {
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) sml[warp * 8 * NT + nt * 8 + gl + j] = make_float2(m_run[nt][j], lsum[nt][j]);
         }
-        if (ctid < G) p.ws_ml[(int64_t)dsc.slot * G + ctid] = sML[ctid];
-      }
-      eok &= epi_sync(&ebar[0], ephase, lane);
-      if (!eok) {
-        if (lane == 0) {
-          raise_flag(p, PAD_FLAG_WAIT_TIMEOUT);
-          *abort_flag = 1;
+        bool eok = consumer_sync(&ebar[0], ephase, lane);
+        float scl[NT][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int g = nt * 8 + gl + j;
+            float M = -INFINITY;
+#pragma unroll
+            for (int ww = 0; ww < WPH; ++ww) M = fmaxf(M, sml[(hl * WPH + ww) * 8 * NT + g].x);
+            const float Mu = (M == -INFINITY) ? 0.f : M;
+            float L = 0.f;
+#pragma unroll
+            for (int ww = 0; ww < WPH; ++ww) {
+              const float2 x = sml[(hl * WPH + ww) * 8 * NT + g];
+              L += x.y * ex2(x.x - Mu);
+            }
+            scl[nt][j] = ex2(m_run[nt][j] - Mu);
+            if (t_base == 0 && (lane >> 2) == 0) sML[hl * 8 * NT + g] = make_float2(Mu, L);
+          }
+        float* buf = epi + hl * (8 * NT * D);
+#pragma unroll
+        for (int step = 0; step < WPH; ++step) {
+          if ((int)(t_base / 16) == step) {
+#pragma unroll
+            for (int mt = 0; mt < KSTEPS; ++mt)
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int d = mt * 16 + (lane >> 2) + (e >= 2 ? 8 : 0);
+                  const int g = nt * 8 + gl + (e & 1);
+                  const float v = acc[mt][nt][e] * scl[nt][e & 1];
+                  if (step == 0) buf[g * D + d] = v;
+                  else buf[g * D + d] += v;
+                }
+          }
+          eok &= consumer_sync(&ebar[0], ephase, lane);
         }
-        return;
+        const int ctid = warp * 32 + lane;
+        if (!split) {
+          __half* obase = p.out + dsc.b * p.out_sb + (int64_t)(dsc.hg * HG * G) * p.out_sh;
+          for (int x = ctid; x < HG * G * (D / 2); x += 32 * kConsumerWarps) {
+            const int row = x / (D / 2), d = (x % (D / 2)) * 2;
+            const int h = row / G, g = row % G;
+            const float L = sML[h * 8 * NT + g].y;
+            const float inv = L > 0.f ? 1.f / L : 0.f;
+            const float* src = epi + h * (8 * NT * D) + g * D + d;
+            *reinterpret_cast<__half2*>(obase + row * p.out_sh + d) = __floats2half2_rn(src[0] * inv, src[1] * inv);
+          }
+        } else {
+          float4* o4 = reinterpret_cast<float4*>(p.ws_o + (int64_t)dsc.slot * HG * G * D);
+          for (int x = ctid; x < HG * G * (D / 4); x += 32 * kConsumerWarps) {
+            const int row = x / (D / 4), d = (x % (D / 4)) * 4;
+            const int h = row / G, g = row % G;
+            o4[x] = *reinterpret_cast<const float4*>(epi + h * (8 * NT * D) + g * D + d);
+          }
+          for (int x = ctid; x < HG * G; x += 32 * kConsumerWarps)
+            p.ws_ml[(int64_t)dsc.slot * HG * G + x] = sML[(x / G) * 8 * NT + x % G];
+        }
+        eok &= consumer_sync(&ebar[0], ephase, lane);
+        if (!eok) {
+          if (lane == 0) {
+            raise_flag(p, PAD_FLAG_WAIT_TIMEOUT);
+            *abort_flag = 1;
+          }
+          return;
+        }
       }
     }
   }
 }
 
-// Phase 2: merge the partials of one split (sequence, KV head) pair for one
-// query row. Grid (partitions, G); partition w works only if it is the first
-// partition of a split pair (ws_meta[w].w == 1).
+// Phase 2: merge the partials of one split (sequence, head group) pair for
+// one (head, query row). Grid (partitions, HG*G); partition w works only if
+// it is the first partition of a split pair (ws_meta[w].w == 1).
 //   M = max_s m_s;  L = sum_s l_s 2^(m_s - M);  O = sum_s O_s 2^(m_s - M) / L
-// (analysis/split_k_derivation.md:44-65; a partial with m_s = -inf weighs 0,
-// the guard of analysis/split_k_derivation.md:67-86).
+// (analysis/split_k_derivation.md:44-65; a partial with m_s = -inf weighs 0
+// and its O is not read, the guard of analysis/split_k_derivation.md:67-86).
 template <int D>
 __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ ws_o, const float2* __restrict__ ws_ml,
                                                     const int4* __restrict__ ws_meta, __half* __restrict__ out,
-                                                    int64_t out_sb, int64_t out_sh, int hkv, int G) {
+                                                    int64_t out_sb, int64_t out_sh, int ngroups, int rows) {
   constexpr int C4 = D / 4;
   constexpr int SG = 256 / C4;
   __shared__ float red[SG][D];
   __shared__ float lred[SG];
   __shared__ float wmax[8];
-  const int w = blockIdx.x, g = blockIdx.y, tid = threadIdx.x;
+  const int w = blockIdx.x, y = blockIdx.y, tid = threadIdx.x;
   const int4 meta = ws_meta[w];
   if (meta.w != 1) return;
   const int pair = meta.x, s0 = meta.y, ns = meta.z;
-  // pass 1: the running max over partials
+  // pass 1: the max over partials
   float mx = -INFINITY;
-  for (int s = tid; s < ns; s += 256) mx = fmaxf(mx, ws_ml[(int64_t)(s0 + s) * G + g].x);
+  for (int s = tid; s < ns; s += 256) mx = fmaxf(mx, ws_ml[(int64_t)(s0 + s) * rows + y].x);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if ((tid & 31) == 0) wmax[tid >> 5] = mx;
@@ -509,9 +598,9 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ ws
   float lsum = 0.f;
 #pragma unroll 4
   for (int s = sg; s < ns; s += SG) {
-    const int64_t row = (int64_t)(s0 + s) * G + g;
+    const int64_t row = (int64_t)(s0 + s) * rows + y;
     const float2 ml = ws_ml[row];
-    if (ml.x == -INFINITY) continue;  // an empty partial: weight 0, its O is not read
+    if (ml.x == -INFINITY) continue;
     const float wt = ex2(ml.x - Mu);
     const float4 o = reinterpret_cast<const float4*>(ws_o + row * D)[c];
     lsum += ml.y * wt;
@@ -536,8 +625,8 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ ws
       L += lred[x];
     }
     const float inv = L > 0.f ? 1.f / L : 0.f;
-    const int b = pair / hkv, h = pair % hkv;
-    __half* o = out + b * out_sb + (int64_t)(h * G + g) * out_sh + tid * 4;
+    const int b = pair / ngroups, hg = pair % ngroups;
+    __half* o = out + b * out_sb + (int64_t)(hg * rows + y) * out_sh + tid * 4;
     reinterpret_cast<__half2*>(o)[0] = __floats2half2_rn(t.x * inv, t.y * inv);
     reinterpret_cast<__half2*>(o)[1] = __floats2half2_rn(t.z * inv, t.w * inv);
   }

@@ -1,8 +1,10 @@
 """Host mirror of the decode kernel's stream-K work partition.
 
-The kernel flattens the batch into one list of 64-token tiles ordered
-(sequence, KV head, tile) and gives partition ``w`` of ``W`` the tiles
-``[floor(w*T/W), floor((w+1)*T/W))``. A (sequence, KV head) pair whose tiles
+The kernel flattens the batch into one list of tiles ordered (sequence, KV
+head group, tile) -- a tile is ``128 / HG`` tokens of ``HG`` KV heads, HG the
+largest of 8, 4, 2, 1 dividing the KV head count (at most 4 when a head has
+more than 8 query rows) -- and gives partition ``w`` of ``W`` the tiles
+``[floor(w*T/W), floor((w+1)*T/W))``. A (sequence, head group) pair whose tiles
 fall in one partition is finished there; a pair spread over several
 partitions gets one fp32 partial per partition, in slots
 ``pair + w`` for ``w`` in ``[owner(first tile), owner(last tile)]``, which the
@@ -16,11 +18,19 @@ from dataclasses import dataclass
 
 import numpy as np
 
-TILE = 64
+TILE_ROWS = 128
 
 
-def tiles_of(seq: int) -> int:
-    return (max(int(seq), 0) + TILE - 1) // TILE
+def head_group(num_kv_heads: int, gqa_ratio: int) -> int:
+    cap = 8 if gqa_ratio <= 8 else 4
+    hg = cap
+    while hg > 1 and num_kv_heads % hg:
+        hg //= 2
+    return hg
+
+
+def tiles_of(seq: int, tt: int = 64) -> int:
+    return (max(int(seq), 0) + tt - 1) // tt
 
 
 def part_begin(w: int, total: int, parts: int) -> int:
@@ -48,27 +58,30 @@ class PairPlan:
         return range(self.pair + self.first_part, self.pair + self.last_part + 1)
 
 
-def plan(seq_lens, num_kv_heads: int, parts: int, cap: int | None = None) -> tuple[int, list[PairPlan]]:
-    """Return (total tiles, per-pair plan) for ``parts`` partitions."""
+def plan(seq_lens, num_groups: int, parts: int, cap: int | None = None, tt: int = 64
+         ) -> tuple[int, list[PairPlan]]:
+    """Return (total tiles, per-pair plan) for ``parts`` partitions over
+    ``num_groups`` head groups per sequence and ``tt``-token tiles."""
     seq = np.asarray(seq_lens, dtype=np.int64)
     if cap is not None:
         seq = np.clip(seq, 0, cap)
-    total = int(sum(tiles_of(s) for s in seq) * num_kv_heads)
+    total = int(sum(tiles_of(s, tt) for s in seq) * num_groups)
     pairs: list[PairPlan] = []
     start = 0
     for b, s in enumerate(seq):
-        n = tiles_of(s)
-        for h in range(num_kv_heads):
+        n = tiles_of(s, tt)
+        for h in range(num_groups):
             if n > 0:
-                pairs.append(PairPlan(b * num_kv_heads + h, start, n, part_owner(start, total, parts),
+                pairs.append(PairPlan(b * num_groups + h, start, n, part_owner(start, total, parts),
                                       part_owner(start + n - 1, total, parts)))
             start += n
     return total, pairs
 
 
-def heuristic_partitions(num_sms: int, ctas_per_sm: int, batch: int, num_kv_heads: int, max_pages: int,
-                         page_size: int) -> int:
+def heuristic_partitions(num_sms: int, ctas_per_sm: int, batch: int, num_kv_heads: int, gqa_ratio: int,
+                         max_pages: int, page_size: int) -> int:
     """The num_splits=None choice: one partition per resident CTA slot,
     capped by the number of tiles the batch can hold."""
-    cap_tiles = batch * num_kv_heads * tiles_of(max_pages * page_size)
+    hg = head_group(num_kv_heads, gqa_ratio)
+    cap_tiles = batch * (num_kv_heads // hg) * tiles_of(max_pages * page_size, TILE_ROWS // hg)
     return max(1, min(num_sms * ctas_per_sm, cap_tiles))

@@ -112,5 +112,7 @@ def test_partition_covers_every_tile_once_with_disjoint_slots(seed, parts):
 
 
 def test_heuristic_partitions():
-    assert partition.heuristic_partitions(148, 2, 64, 2, 256, 16) == 296
-    assert partition.heuristic_partitions(148, 2, 1, 2, 1, 16) == 2  # tiny batch: one per tile
+    assert partition.heuristic_partitions(148, 1, 64, 2, 6, 256, 16) == 148
+    assert partition.heuristic_partitions(148, 1, 1, 2, 6, 1, 16) == 1  # tiny batch: one per tile
+    assert partition.head_group(8, 4) == 8 and partition.head_group(2, 6) == 2 and partition.head_group(6, 1) == 2
+    assert partition.head_group(8, 16) == 4 and partition.head_group(3, 2) == 1

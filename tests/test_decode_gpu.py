@@ -222,3 +222,19 @@ def test_full_size_properties_c2_b64_on_device():
     for b in (0, 31, 63):
         solo = pad_b200.paged_attention_decode_cuda_v4(q[b:b + 1], k, v, bt[b:b + 1], sl[b:b + 1])
         torch.testing.assert_close(solo.float(), o1[b:b + 1].float(), rtol=1e-2, atol=2e-3)
+
+
+@pytest.mark.parametrize("hkv", [1, 2, 4, 8])
+@pytest.mark.parametrize("head_dim", [32, 64, 128])
+@pytest.mark.parametrize("page_size", [1, 4, 16])
+def test_head_group_page_split_matrix(hkv, head_dim, page_size):
+    """Every head-group width (8/4/2/1 KV heads per tile) on the swizzled and
+    unswizzled paths, with split counts that make partitions start on the last
+    (partial) tile of one sequence and continue into the next -- the pattern
+    that exercises the single-slot query ring."""
+    seqs = [228, 183, 376, 95, 160]
+    c = explicit_case(seqs, num_kv_heads=hkv, gqa_ratio=4, head_dim=head_dim, page_size=page_size,
+                      seed=hkv * 100 + head_dim + page_size)
+    ref = oracle.decode_c(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens)
+    for s in (None, 1, 2, 3, 4, 5, 6, 7, 9):
+        assert_parity(run(c, num_splits=s), ref, f"hkv={hkv} D={head_dim} ps={page_size} S={s}")
