@@ -114,6 +114,33 @@ int pad_paged_attention_decode(const void* q, const void* k_cache, const void* v
                                int64_t num_splits, void* workspace, size_t workspace_bytes,
                                void* stream, int32_t* error_flags);
 
+/* Decode without any device allocation, for callers that cannot call
+ * cudaMalloc: code running inside a CUDA stream capture they do not own,
+ * embedders whose memory is owned by a custom allocator or a fixed arena,
+ * and real-time paths where an allocation could block. It behaves exactly
+ * like pad_paged_attention_decode (same arguments minus the workspace) but
+ * keeps the split partials in a scratch array built into the library,
+ * PAD_STATIC_SCRATCH_BYTES (16 MiB) per GPU, which every GPU that loads the
+ * library holds until the process exits. Problems whose workspace
+ * (pad_decode_workspace_bytes) exceeds that size are rejected with
+ * PAD_ERR_WORKSPACE. The first call on a device looks up the scratch
+ * array's device address (cudaGetSymbolAddress) with that device current,
+ * so make that first call before any stream capture. All calls on a device
+ * share the one array: calls that overlap on the GPU (different streams, no
+ * ordering between them) race and must be avoided. Nothing in the array has
+ * to start zeroed; each call rewrites what it reads.
+ * No counterpart in the reference. */
+#define PAD_STATIC_SCRATCH_BYTES ((size_t)16 << 20)
+int pad_paged_attention_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                       const int32_t* block_table, const int32_t* seq_lens, void* out,
+                                       int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
+                                       int64_t head_dim, int64_t num_pages, int64_t page_size,
+                                       int64_t max_pages_per_seq, const int64_t* q_strides,
+                                       const int64_t* k_strides, const int64_t* v_strides,
+                                       int64_t block_table_stride, const int64_t* out_strides,
+                                       float scale, int64_t num_splits, void* stream,
+                                       int32_t* error_flags);
+
 #ifdef __cplusplus
 }
 #endif

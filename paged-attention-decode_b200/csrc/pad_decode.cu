@@ -406,4 +406,55 @@ int pad_paged_attention_decode(const void* q, const void* k_cache, const void* v
   return PAD_OK;
 }
 
+// ----------------------------------------------------------------- no-alloc entry
+// Scratch for pad_paged_attention_decode_noalloc, part of the library image:
+// the driver reserves it on every GPU the library is loaded on.
+static __device__ __align__(256) uint8_t g_pad_static_scratch[PAD_STATIC_SCRATCH_BYTES];
+
+int pad_paged_attention_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                       const int32_t* block_table, const int32_t* seq_lens, void* out,
+                                       int64_t batch, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
+                                       int64_t num_pages, int64_t page_size, int64_t max_pages_per_seq,
+                                       const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                                       int64_t block_table_stride, const int64_t* out_strides, float scale,
+                                       int64_t num_splits, void* stream, int32_t* error_flags) {
+  // In host code g_pad_static_scratch names a host-side shadow, not device
+  // memory; the device address comes from cudaGetSymbolAddress, looked up
+  // once per device with that device current and cached.
+  static void* scratch_ptr[kMaxDevices] = {};
+  static std::mutex mu;
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (device < 0 || device >= kMaxDevices) return fail(PAD_ERR_INVALID_ARGUMENT, "device %d out of range", device);
+  void* ptr = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (scratch_ptr[device] == nullptr) {
+      e = cudaGetSymbolAddress(&scratch_ptr[device], g_pad_static_scratch);
+      if (e != cudaSuccess) {
+        scratch_ptr[device] = nullptr;
+        return cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
+      }
+    }
+    ptr = scratch_ptr[device];
+  }
+  if (batch > 0 && num_q_heads > 0 && num_kv_heads > 0 && num_q_heads % num_kv_heads == 0 && num_pages > 0 &&
+      max_pages_per_seq > 0) {
+    size_t need = 0;
+    const int st = pad_decode_workspace_bytes(device, batch, num_kv_heads, num_q_heads / num_kv_heads, head_dim,
+                                              page_size, max_pages_per_seq, num_splits, &need);
+    if (st != PAD_OK) return st;
+    if (need > PAD_STATIC_SCRATCH_BYTES)
+      return fail(PAD_ERR_WORKSPACE,
+                  "problem needs %zu bytes of scratch, more than the %zu-byte static scratch of the no-alloc "
+                  "entry point; use pad_paged_attention_decode with a caller-provided workspace",
+                  need, (size_t)PAD_STATIC_SCRATCH_BYTES);
+  }
+  return pad_paged_attention_decode(q, k_cache, v_cache, block_table, seq_lens, out, batch, num_q_heads,
+                                    num_kv_heads, head_dim, num_pages, page_size, max_pages_per_seq, q_strides,
+                                    k_strides, v_strides, block_table_stride, out_strides, scale, num_splits, ptr,
+                                    PAD_STATIC_SCRATCH_BYTES, stream, error_flags);
+}
+
 }  // extern "C"

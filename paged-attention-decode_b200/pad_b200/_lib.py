@@ -39,7 +39,13 @@ SIGNATURES = {
     "pad_paged_attention_decode": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp] + [_c_i64] * 7
                                    + [_c_i64p, _c_i64p, _c_i64p, _c_i64, _c_i64p, ctypes.c_float, _c_i64,
                                       _vp, ctypes.c_size_t, _vp, _vp]),
+    "pad_paged_attention_decode_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp] + [_c_i64] * 7
+                                           + [_c_i64p, _c_i64p, _c_i64p, _c_i64, _c_i64p, ctypes.c_float,
+                                              _c_i64, _vp, _vp]),
 }
+
+# Bytes of the library's built-in scratch used by pad_paged_attention_decode_noalloc.
+PAD_STATIC_SCRATCH_BYTES = 16 << 20
 
 _lib = None
 
