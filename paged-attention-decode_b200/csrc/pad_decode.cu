@@ -39,7 +39,8 @@ int cuda_fail(cudaError_t e, const char* what) {
 // ----------------------------------------------------------------- instances
 struct Instance {
   const void* kernel;          // decode_stream_kernel<TR>
-  const void* merge;           // merge_kernel<D>
+  const void* merge_small;     // merge_kernel<D, 128>: few partials per split pair
+  const void* merge_large;     // merge_kernel<D, 512>: many partials (long context)
   int smem_bytes;
   int segw;                    // bytes per row segment (TMA box inner extent)
   bool swz;
@@ -52,7 +53,8 @@ Instance make_instance() {
   using TR = Traits<D, NT, HG, SWZ>;
   Instance in;
   in.kernel = reinterpret_cast<const void*>(&decode_stream_kernel<TR>);
-  in.merge = reinterpret_cast<const void*>(&merge_kernel<D>);
+  in.merge_small = reinterpret_cast<const void*>(&merge_kernel<D, 128>);
+  in.merge_large = reinterpret_cast<const void*>(&merge_kernel<D, 512>);
   in.smem_bytes = TR::SMEM_BYTES;
   in.segw = TR::SEGW;
   in.swz = SWZ;
@@ -400,7 +402,20 @@ int pad_paged_attention_decode(const void* q, const void* k_cache, const void* v
     __half* a3 = prm.out;
     int ngroups = (int)(num_kv_heads / in.hg), rows = (int)(gqa * in.hg);
     void* margs[] = {&a0, &a1, &a2, &a3, &prm.out_sb, &prm.out_sh, &ngroups, &rows};
-    e = cudaLaunchKernel(in.merge, dim3((unsigned)plan.partitions, (unsigned)rows), dim3(256), margs, 0, s);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)plan.partitions, (unsigned)rows);
+    // A split pair has about partitions / pairs partials: fold a handful with a
+    // small block, long-context splits (hundreds of partials) with a wide one.
+    const bool wide = plan.partitions > 4 * batch * ngroups;
+    cfg.blockDim = dim3(wide ? 512 : 128);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // overlap its launch with the decode tail
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelExC(&cfg, wide ? in.merge_large : in.merge_small, margs);
     if (e != cudaSuccess) return cuda_fail(e, "launching the merge kernel");
   }
   return PAD_OK;
@@ -456,5 +471,12 @@ int pad_paged_attention_decode_noalloc(const void* q, const void* k_cache, const
                                     k_strides, v_strides, block_table_stride, out_strides, scale, num_splits, ptr,
                                     PAD_STATIC_SCRATCH_BYTES, stream, error_flags);
 }
+
+#ifdef PAD_TRACE
+int pad_debug_trace_read(uint64_t* host, size_t n) {
+  cudaError_t e = cudaMemcpyFromSymbol(host, g_pad_trace, n * sizeof(uint64_t));
+  return e == cudaSuccess ? PAD_OK : cuda_fail(e, "trace read");
+}
+#endif
 
 }  // extern "C"

@@ -11,6 +11,14 @@ __device__ __forceinline__ void raise_flag(const DecodeParams& p, int bits) {
   if (p.error_flags != nullptr) atomicOr(p.error_flags, bits);
 }
 
+#ifdef PAD_TRACE
+// Development-only timeline: per-CTA %globaltimer stamps (compile with -DPAD_TRACE).
+__device__ uint64_t g_pad_trace[4096 * 8];
+#define PAD_STAMP(i) (g_pad_trace[blockIdx.x * 8 + (i)] = globaltimer_ns())
+#else
+#define PAD_STAMP(i) ((void)0)
+#endif
+
 template <class TR>
 __device__ __forceinline__ int tiles_of(int seq) {
   return (seq + TR::TT - 1) / TR::TT;
@@ -62,7 +70,7 @@ __device__ __forceinline__ void store_page_ids(int* slot_ids, int lane, const in
 __device__ __forceinline__ bool consumer_sync(uint64_t* bar, uint32_t& phase, int lane) {
   __syncwarp();
   if (lane == 0) mbar_arrive(bar);
-  const bool ok = mbar_wait_bounded(bar, phase, kWaitTimeoutNs);
+  const bool ok = mbar_spin_bounded(bar, phase, kWaitTimeoutNs);
   phase ^= 1u;
   __syncwarp();
   return ok;
@@ -97,6 +105,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
   const int w = blockIdx.x;
   const int G = p.gqa;
   const int ngroups = p.hkv / HG;
+  if (tid == 0) PAD_STAMP(0);
 
   // ---- set-up: zero the query tiles (rows past HG*G stay zero), init barriers
   for (int x = tid; x < TR::QSLOTS * TR::Q_BYTES / 16; x += kThreads)
@@ -164,6 +173,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
   }
   fence_proxy_async_smem();  // zeroed query tiles before any TMA write to them
   __syncthreads();
+  if (tid == 0) PAD_STAMP(1);
+  // the merge kernel may be scheduled now; it waits for this grid's results
+  if (tid == 0) pdl_launch_dependents();
 
   // ---- zero output rows of empty sequences (src/reference.py:32-34)
   for (int b = w; b < p.batch; b += (int)W) {
@@ -276,6 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
           tma_load_4d(st + TR::KT_BYTES + off, &p.tm_v, &full[s], sg * (TR::SEGW / 2), row, c.hg * HG, page);
         }
       }
+      if (k == 0 && lane == 0) PAD_STAMP(2);
       ++issued;
       if (first) ++segs;
       if (k + S < ntiles) {
@@ -364,6 +377,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     }
     const uint32_t kb = smem_u32(stages + s * TR::STAGE_BYTES);
     const uint32_t vb = kb + TR::KT_BYTES;
+    if (k == 0 && warp == 0 && lane == 0) PAD_STAMP(3);
+    if (k == ntiles - 1 && warp == 0 && lane == 0) PAD_STAMP(4);
 
     const int nv = min(16, dsc.seq - (dsc.i * TT + (int)t_base));
     if (nv > 0) {
@@ -509,6 +524,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
             scl[nt][j] = ex2(m_run[nt][j] - Mu);
             if (t_base == 0 && (lane >> 2) == 0) sML[hl * 8 * NT + g] = make_float2(Mu, L);
           }
+        // the WPH warps of a head add their rescaled O^T into one buffer in a
+        // fixed order (deterministic results): warp 0 stores, the others add
         float* buf = epi + hl * (8 * NT * D);
 #pragma unroll
         for (int step = 0; step < WPH; ++step) {
@@ -519,11 +536,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
               for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                  const int d = mt * 16 + (lane >> 2) + (e >= 2 ? 8 : 0);
-                  const int g = nt * 8 + gl + (e & 1);
+                  const int idx = (nt * 8 + gl + (e & 1)) * D + mt * 16 + (lane >> 2) + (e >= 2 ? 8 : 0);
                   const float v = acc[mt][nt][e] * scl[nt][e & 1];
-                  if (step == 0) buf[g * D + d] = v;
-                  else buf[g * D + d] += v;
+                  if (step == 0) buf[idx] = v;
+                  else buf[idx] += v;
                 }
           }
           eok &= consumer_sync(&ebar[0], ephase, lane);
@@ -549,7 +565,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
           for (int x = ctid; x < HG * G; x += 32 * kConsumerWarps)
             p.ws_ml[(int64_t)dsc.slot * HG * G + x] = sML[(x / G) * 8 * NT + x % G];
         }
-        eok &= consumer_sync(&ebar[0], ephase, lane);
+        // No trailing sync: the next epilogue's first sync orders these reads
+        // before any warp writes the buffer again.
         if (!eok) {
           if (lane == 0) {
             raise_flag(p, PAD_FLAG_WAIT_TIMEOUT);
@@ -560,6 +577,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
       }
     }
   }
+  if (warp == 0 && lane == 0) PAD_STAMP(5);
 }
 
 // Phase 2: merge the partials of one split (sequence, head group) pair for
@@ -568,61 +586,76 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
 //   M = max_s m_s;  L = sum_s l_s 2^(m_s - M);  O = sum_s O_s 2^(m_s - M) / L
 // (analysis/split_k_derivation.md:44-65; a partial with m_s = -inf weighs 0
 // and its O is not read, the guard of analysis/split_k_derivation.md:67-86).
-template <int D>
-__global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ ws_o, const float2* __restrict__ ws_ml,
-                                                    const int4* __restrict__ ws_meta, __half* __restrict__ out,
-                                                    int64_t out_sb, int64_t out_sh, int ngroups, int rows) {
-  constexpr int C4 = D / 4;
-  constexpr int SG = 256 / C4;
-  __shared__ float red[SG][D];
-  __shared__ float lred[SG];
-  __shared__ float wmax[8];
+// Each thread folds a strided subset of the partials with an online LSE
+// (loads issued four at a time), then the per-thread states are combined
+// through shared memory. Launched as a programmatic dependent of the decode
+// kernel: it waits on griddepcontrol before reading the partials.
+template <int D, int kMergeThreads>
+__global__ void __launch_bounds__(kMergeThreads) merge_kernel(const float* __restrict__ ws_o,
+                                                              const float2* __restrict__ ws_ml,
+                                                              const int4* __restrict__ ws_meta,
+                                                              __half* __restrict__ out, int64_t out_sb,
+                                                              int64_t out_sh, int ngroups, int rows) {
+  constexpr int C4 = D / 4;                // float4 columns of one partial row
+  constexpr int PG = kMergeThreads / C4;   // partial groups folded in parallel
+  __shared__ float red_o[PG][D];
+  __shared__ float red_m[PG], red_l[PG];
+  pdl_wait_primary();
   const int w = blockIdx.x, y = blockIdx.y, tid = threadIdx.x;
   const int4 meta = ws_meta[w];
   if (meta.w != 1) return;
   const int pair = meta.x, s0 = meta.y, ns = meta.z;
-  // pass 1: the max over partials
-  float mx = -INFINITY;
-  for (int s = tid; s < ns; s += 256) mx = fmaxf(mx, ws_ml[(int64_t)(s0 + s) * rows + y].x);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if ((tid & 31) == 0) wmax[tid >> 5] = mx;
-  __syncthreads();
-  float M = wmax[0];
-#pragma unroll
-  for (int x = 1; x < 8; ++x) M = fmaxf(M, wmax[x]);
-  const float Mu = (M == -INFINITY) ? 0.f : M;
-  // pass 2: weighted sums, partials strided over SG groups
   const int c = tid % C4, sg = tid / C4;
+  float m = -INFINITY, l = 0.f;
   float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-  float lsum = 0.f;
-#pragma unroll 4
-  for (int s = sg; s < ns; s += SG) {
-    const int64_t row = (int64_t)(s0 + s) * rows + y;
-    const float2 ml = ws_ml[row];
-    if (ml.x == -INFINITY) continue;
-    const float wt = ex2(ml.x - Mu);
-    const float4 o = reinterpret_cast<const float4*>(ws_o + row * D)[c];
-    lsum += ml.y * wt;
-    a.x += o.x * wt;
-    a.y += o.y * wt;
-    a.z += o.z * wt;
-    a.w += o.w * wt;
+  for (int s = sg; s < ns; s += 4 * PG) {
+    float2 ml[4];
+    float4 o[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int su = s + u * PG;
+      ml[u] = make_float2(-INFINITY, 0.f);
+      if (su < ns) {
+        const int64_t row = (int64_t)(s0 + su) * rows + y;
+        ml[u] = ws_ml[row];
+        o[u] = reinterpret_cast<const float4*>(ws_o + row * D)[c];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (ml[u].x == -INFINITY) continue;
+      const float mn = fmaxf(m, ml[u].x);
+      const float al = ex2(m - mn), be = ex2(ml[u].x - mn);
+      l = l * al + ml[u].y * be;
+      a.x = a.x * al + o[u].x * be;
+      a.y = a.y * al + o[u].y * be;
+      a.z = a.z * al + o[u].z * be;
+      a.w = a.w * al + o[u].w * be;
+      m = mn;
+    }
   }
-  *reinterpret_cast<float4*>(&red[sg][c * 4]) = a;
-  if (c == 0) lred[sg] = lsum;
+  *reinterpret_cast<float4*>(&red_o[sg][c * 4]) = a;
+  if (c == 0) {
+    red_m[sg] = m;
+    red_l[sg] = l;
+  }
   __syncthreads();
   if (tid < C4) {
+    float M = -INFINITY;
+#pragma unroll 8
+    for (int x = 0; x < PG; ++x) M = fmaxf(M, red_m[x]);
+    const float Mu = (M == -INFINITY) ? 0.f : M;
     float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
     float L = 0.f;
-#pragma unroll
-    for (int x = 0; x < SG; ++x) {
-      const float4 v = *reinterpret_cast<const float4*>(&red[x][tid * 4]);
-      t.x += v.x;
-      t.y += v.y;
-      t.z += v.z;
-      t.w += v.w;
-      L += lred[x];
+#pragma unroll 8
+    for (int x = 0; x < PG; ++x) {
+      const float wt = ex2(red_m[x] - Mu);  // 0 for groups that saw no partial
+      const float4 v = *reinterpret_cast<const float4*>(&red_o[x][tid * 4]);
+      t.x += v.x * wt;
+      t.y += v.y * wt;
+      t.z += v.z * wt;
+      t.w += v.w * wt;
+      L += red_l[x] * wt;
     }
     const float inv = L > 0.f ? 1.f / L : 0.f;
     const int b = pair / ngroups, hg = pair % ngroups;
