@@ -15,8 +15,12 @@ __device__ __forceinline__ void raise_flag(const DecodeParams& p, int bits) {
 // Development-only timeline: per-CTA %globaltimer stamps (compile with -DPAD_TRACE).
 __device__ uint64_t g_pad_trace[4096 * 8];
 #define PAD_STAMP(i) (g_pad_trace[blockIdx.x * 8 + (i)] = globaltimer_ns())
+#define PAD_STAMP_MIN(i) atomicMin((unsigned long long*)&g_pad_trace[4096 * 8 - 2 + (i)], (unsigned long long)globaltimer_ns())
+#define PAD_STAMP_MAX(i) atomicMax((unsigned long long*)&g_pad_trace[4096 * 8 - 2 + (i)], (unsigned long long)globaltimer_ns())
 #else
 #define PAD_STAMP(i) ((void)0)
+#define PAD_STAMP_MIN(i) ((void)0)
+#define PAD_STAMP_MAX(i) ((void)0)
 #endif
 
 template <class TR>
@@ -65,16 +69,12 @@ __device__ __forceinline__ void store_page_ids(int* slot_ids, int lane, const in
     if (lane + 32 * u < TR::NB_MAX) slot_ids[lane + 32 * u] = v[u];
 }
 
-// Cross-warp sync of the consumer warps on an mbarrier (count = consumer
-// warps) with a bounded wait. Returns false on timeout.
-__device__ __forceinline__ bool consumer_sync(uint64_t* bar, uint32_t& phase, int lane) {
-  __syncwarp();
-  if (lane == 0) mbar_arrive(bar);
-  const bool ok = mbar_spin_bounded(bar, phase, kWaitTimeoutNs);
-  phase ^= 1u;
-  __syncwarp();
-  return ok;
-}
+// Named barriers of the consumer warps (ids 1 and 2; 0 is __syncthreads).
+// Safe from deadlock because consumer warps only ever leave the tile loop
+// together: every exit decision goes through consumer_vote first.
+constexpr uint32_t kConsumerThreads = 32 * kConsumerWarps;
+__device__ __forceinline__ void consumer_sync() { named_barrier(1, kConsumerThreads); }
+__device__ __forceinline__ bool consumer_vote(bool ok) { return named_barrier_and(2, kConsumerThreads, ok); }
 
 template <class TR>
 __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid_constant__ DecodeParams p) {
@@ -123,6 +123,26 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     *abort_flag = 0;
     cur_smem[0] = -1;
     fence_mbar_init();
+  }
+
+  // ---- speculative page ids: the producer guesses its first tiles assuming
+  // every sequence fills its block-table row (true for uniform batches) and
+  // loads their page ids now, overlapping the seq_lens round trip below.
+  const int ncap = tiles_of<TR>(cap);
+  const int64_t tg_total = (int64_t)p.batch * ngroups * ncap;
+  const int tg0 = tg_total > 0 ? part_begin(w, tg_total, W) : 0;
+  int gpid[S][TR::NB_PER_LANE];
+  if (warp == kConsumerWarps) {
+#pragma unroll
+    for (int k = 0; k < S; ++k) {
+      const int64_t t = (int64_t)tg0 + k;
+      if (t < tg_total) {
+        const int per_seq = ngroups * ncap;
+        const int r = (int)(t % per_seq);
+        const Cursor gc{(int)(t / per_seq), r / ncap, r % ncap, ncap, cap, 0};
+        load_page_ids<TR>(p, gc, lane, gpid[k]);
+      }
+    }
   }
 
   // ---- block-wide exclusive scan of tiles per sequence (x head groups)
@@ -207,10 +227,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     Cursor c{cur_smem[0], cur_smem[1], cur_smem[2], cur_smem[3], cur_smem[4], cur_smem[5]};
     Cursor la = c;
     int pid[S][TR::NB_PER_LANE];
+    const int per_seq = ngroups * ncap;
 #pragma unroll
     for (int k = 0; k < S; ++k) {
       if (k < ntiles) {
-        load_page_ids<TR>(p, la, lane, pid[k]);
+        // reuse the speculative ids when the real tile is the guessed one
+        const int64_t t = (int64_t)tg0 + k;
+        const bool hit = t < tg_total && la.b == (int)(t / per_seq) && la.hg == (int)(t % per_seq) / ncap &&
+                         la.i == (int)(t % per_seq) % ncap;
+        if (hit) {
+#pragma unroll
+          for (int u = 0; u < TR::NB_PER_LANE; ++u) pid[k][u] = gpid[k][u];
+        } else {
+          load_page_ids<TR>(p, la, lane, pid[k]);
+        }
         cursor_next<TR>(la, p, cap, ngroups);
       }
     }
@@ -322,7 +352,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
   uint32_t qf[KSTEPS][NT][2];
   float acc[KSTEPS][NT][4];
   float m_run[NT][2], l_run[NT][2];
-  uint32_t ephase = 0;
   int segs = 0;
 
   for (int k = 0; k < ntiles; ++k) {
@@ -368,8 +397,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
           for (int e = 0; e < 4; ++e) acc[mt][nt][e] = 0.f;
       }
     }
-    if (!__all_sync(0xffffffffu, ok) || *abort_flag) {
-      if (lane == 0) {
+    // collective go/no-go: all consumer warps continue or all leave
+    if (!consumer_vote(ok && !*abort_flag)) {
+      if (warp == 0 && lane == 0) {
         raise_flag(p, PAD_FLAG_WAIT_TIMEOUT);
         *abort_flag = 1;
       }
@@ -460,6 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     if (lane == 0) mbar_arrive(&empty[s]);
 
     if (dsc.flags & kLast) {
+      if (warp == 0 && lane == 0) PAD_STAMP(6);
       // ------------- segment epilogue: merge the WPH warps of each head, write
       // the fp16 output rows (pair finished here) or the fp32 partial (split pair)
       float lsum[NT][2];
@@ -504,7 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
 #pragma unroll
             for (int j = 0; j < 2; ++j) sml[warp * 8 * NT + nt * 8 + gl + j] = make_float2(m_run[nt][j], lsum[nt][j]);
         }
-        bool eok = consumer_sync(&ebar[0], ephase, lane);
+        consumer_sync();
         float scl[NT][2];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
@@ -542,8 +573,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
                   else buf[idx] += v;
                 }
           }
-          eok &= consumer_sync(&ebar[0], ephase, lane);
+          consumer_sync();
         }
+        if (warp == 0 && lane == 0) PAD_STAMP(7);
         const int ctid = warp * 32 + lane;
         if (!split) {
           __half* obase = p.out + dsc.b * p.out_sb + (int64_t)(dsc.hg * HG * G) * p.out_sh;
@@ -567,13 +599,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
         }
         // No trailing sync: the next epilogue's first sync orders these reads
         // before any warp writes the buffer again.
-        if (!eok) {
-          if (lane == 0) {
-            raise_flag(p, PAD_FLAG_WAIT_TIMEOUT);
-            *abort_flag = 1;
-          }
-          return;
-        }
       }
     }
   }
@@ -602,6 +627,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const float* __res
   __shared__ float red_m[PG], red_l[PG];
   pdl_wait_primary();
   const int w = blockIdx.x, y = blockIdx.y, tid = threadIdx.x;
+  if (tid == 0) PAD_STAMP_MIN(0);
   const int4 meta = ws_meta[w];
   if (meta.w != 1) return;
   const int pair = meta.x, s0 = meta.y, ns = meta.z;
@@ -662,6 +688,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const float* __res
     __half* o = out + b * out_sb + (int64_t)(hg * rows + y) * out_sh + tid * 4;
     reinterpret_cast<__half2*>(o)[0] = __floats2half2_rn(t.x * inv, t.y * inv);
     reinterpret_cast<__half2*>(o)[1] = __floats2half2_rn(t.z * inv, t.w * inv);
+    if (tid == 0) PAD_STAMP_MAX(1);
   }
 }
 

@@ -165,6 +165,21 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Named barrier with an AND-vote: every participating thread gets the AND
+// of all threads' `pred`.
+__device__ __forceinline__ bool named_barrier_and(uint32_t id, uint32_t count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.and.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
 // Named barrier over `count` threads (ids 1.. are free for the kernels).
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
