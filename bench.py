@@ -150,7 +150,8 @@ def make_pools(cfg, batch, seq_len, seq_lens, device, min_bytes):
 
     first = config_case(cfg, batch=batch, seq_len=seq_len, seq_lens=seq_lens, device=device, seed=0)
     per = kv_bytes(first.seq_lens.cpu().numpy(), first.k_cache.shape[2], first.k_cache.shape[3])
-    n = max(2, min(64, math.ceil(min_bytes / max(per, 1))))
+    # one pool is enough once a single step streams well past L2 (C5: ~36 GB)
+    n = 1 if per >= min_bytes else max(2, min(64, math.ceil(min_bytes / max(per, 1))))
     pools = [first] + [config_case(cfg, batch=batch, seq_len=seq_len, seq_lens=seq_lens, device=device, seed=i)
                        for i in range(1, n)]
     return pools, per
@@ -292,6 +293,40 @@ def cpu_baseline_sample(pool, seconds: float = 10.0):
                       f"(oracle/pa_oracle.c) on {threads} host threads"}
 
 
+def check_and_gather(pool, world, rank, torch):
+    """C5 bookkeeping outside the timed region: every rank checks sampled
+    sequences of its shard against the C oracle (their pages copied into a
+    compact host pool), and the outputs are gathered to rank 0 over NCCL."""
+    import oracle
+    import pad_b200
+    from pad_b200.sharded import localize
+
+    out = pad_b200.paged_attention_decode_cuda_v4(pool.q, pool.k_cache, pool.v_cache, pool.block_table,
+                                                  pool.seq_lens)
+    idx = np.random.default_rng(rank).choice(pool.q.shape[0], 4, replace=False)
+    ti = torch.from_numpy(idx).cuda()
+    sub = localize(pool.q[ti], pool.k_cache, pool.v_cache, pool.block_table[ti], pool.seq_lens[ti], 1, 0,
+                   device="cpu")
+    ref = oracle.decode_c(sub.q.numpy(), sub.k_cache.numpy(), sub.v_cache.numpy(), sub.block_table.numpy(),
+                          sub.seq_lens.numpy())
+    err = torch.tensor([float(np.abs(out[ti].float().cpu().numpy() - ref).max())], device="cuda")
+    res = {}
+    if world > 1:
+        import torch.distributed as dist
+        from pad_b200.sharded import gather_to_rank0
+
+        dist.all_reduce(err, op=dist.ReduceOp.MAX)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        full = gather_to_rank0(out, pool.q.shape[0] * world, world)
+        torch.cuda.synchronize()
+        res["gather_to_rank0"] = {"ms": (time.perf_counter() - t0) * 1e3,
+                                  "rows": None if full is None else int(full.shape[0])}
+    res["check"] = {"sampled_sequences_per_rank": 4, "max_abs_err_vs_oracle": float(err.item()),
+                    "tolerance": "2e-3 + 1e-2*|ref|"}
+    return res
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -329,6 +364,8 @@ def run_ours(args):
     traffic = committed_traffic() if cfg == "c2" and batch == 64 else None
 
     extra = {}
+    if cfg == "c5" and not args.no_extras:
+        extra.update(check_and_gather(pools[0], world, rank, torch))
     if args.no_extras:
         args.no_sweep = True
     if rank == 0 and not args.no_extras:
