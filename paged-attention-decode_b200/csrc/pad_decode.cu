@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -40,7 +41,8 @@ int cuda_fail(cudaError_t e, const char* what) {
 struct Instance {
   const void* kernel;          // decode_stream_kernel<TR>
   const void* merge_small;     // merge_kernel<D, 128>: few partials per split pair
-  const void* merge_large;     // merge_kernel<D, 512>: many partials (long context)
+  const void* merge_large;     // merge_kernel<D, 256, D/32>: many partials (long context), D split over CTAs
+  int merge_dsplit;
   int smem_bytes;
   int segw;                    // bytes per row segment (TMA box inner extent)
   bool swz;
@@ -53,8 +55,9 @@ Instance make_instance() {
   using TR = Traits<D, NT, HG, SWZ>;
   Instance in;
   in.kernel = reinterpret_cast<const void*>(&decode_stream_kernel<TR>);
-  in.merge_small = reinterpret_cast<const void*>(&merge_kernel<D, 128>);
-  in.merge_large = reinterpret_cast<const void*>(&merge_kernel<D, 512>);
+  in.merge_small = reinterpret_cast<const void*>(&merge_kernel<D, 128, 1>);
+  in.merge_large = reinterpret_cast<const void*>(&merge_kernel<D, 256, (D >= 64 ? D / 32 : 1)>);
+  in.merge_dsplit = D >= 64 ? D / 32 : 1;
   in.smem_bytes = TR::SMEM_BYTES;
   in.segw = TR::SEGW;
   in.swz = SWZ;
@@ -203,7 +206,7 @@ int make_plan(int device, int64_t batch, int64_t hkv, int64_t gqa, int64_t head_
   plan->partitions = parts;
   plan->slots = parts + batch * groups;
   plan->off_meta = 0;
-  plan->off_ml = align_up((size_t)parts * sizeof(int4), 256);
+  plan->off_ml = align_up((size_t)std::max<int64_t>(parts, batch * groups) * sizeof(int4), 256);
   plan->off_o = align_up(plan->off_ml + (size_t)plan->slots * hg * gqa * sizeof(float2), 256);
   plan->bytes = align_up(plan->off_o + (size_t)plan->slots * hg * gqa * head_dim * sizeof(float), 256);
   return PAD_OK;
@@ -389,6 +392,7 @@ int pad_paged_attention_decode(const void* q, const void* k_cache, const void* v
   prm.num_pages = (int)num_pages;
   prm.max_pages = (int)max_pages_per_seq;
   prm.box_rows = plan.box_rows;
+  prm.meta_by_pair = batch * (num_kv_heads / in.hg) < plan.partitions ? 1 : 0;
   prm.scale_log2 = scale * kLog2e;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -403,11 +407,12 @@ int pad_paged_attention_decode(const void* q, const void* k_cache, const void* v
     int ngroups = (int)(num_kv_heads / in.hg), rows = (int)(gqa * in.hg);
     void* margs[] = {&a0, &a1, &a2, &a3, &prm.out_sb, &prm.out_sh, &ngroups, &rows};
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)plan.partitions, (unsigned)rows);
+    const bool wide = plan.partitions > 4 * batch * ngroups;
+    const int64_t merge_x = prm.meta_by_pair ? batch * ngroups : plan.partitions;
+    cfg.gridDim = dim3((unsigned)merge_x, (unsigned)rows, wide ? (unsigned)in.merge_dsplit : 1u);
     // A split pair has about partitions / pairs partials: fold a handful with a
     // small block, long-context splits (hundreds of partials) with a wide one.
-    const bool wide = plan.partitions > 4 * batch * ngroups;
-    cfg.blockDim = dim3(wide ? 512 : 128);
+    cfg.blockDim = dim3(wide ? 256 : 128);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];

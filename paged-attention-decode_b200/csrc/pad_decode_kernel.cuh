@@ -37,6 +37,7 @@ constexpr int kThreads = 32 * (kConsumerWarps + 1);
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s: no legitimate wait comes close
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kSmemBudget = 227 * 1024;
+constexpr int kSeqCache = 1024;   // seq_lens kept in shared memory when batch <= this
 
 struct __align__(64) DecodeParams {
   CUtensorMap tm_k;  // dims {D, page_size, Hkv, num_pages}, box {SEG, R, HG, 1}
@@ -53,6 +54,7 @@ struct __align__(64) DecodeParams {
   int64_t out_sb, out_sh;
   int batch, hkv, gqa, page_size, num_pages, max_pages;
   int box_rows;      // R: tokens per TMA box (divides page_size and TT)
+  int meta_by_pair;  // merge descriptors indexed by pair (else by partition)
   float scale_log2;  // scale * log2(e)
 };
 
@@ -81,7 +83,7 @@ struct Traits {
   static constexpr int NB_PER_LANE = (NB_MAX + 31) / 32;
   // Cross-warp merge buffer (only when several warps share a head).
   static constexpr int EPI_BYTES = WPH > 1 ? HG * 8 * NT * D * 4 : 0;
-  static constexpr int MISC_BYTES = 4096;
+  static constexpr int MISC_BYTES = 4096 + kSeqCache * 4;  // + cached seq_lens
   // Query tiles in flight: two (one segment ahead) unless that costs a stage.
   static constexpr int QSLOTS = (kSmemBudget - (1024 + 2 * Q_BYTES + EPI_BYTES + MISC_BYTES)) / STAGE_BYTES >= 3 ? 2 : 1;
   static constexpr int FIXED_BYTES = 1024 /*align slack*/ + QSLOTS * Q_BYTES + EPI_BYTES + MISC_BYTES;

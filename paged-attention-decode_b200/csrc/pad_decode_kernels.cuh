@@ -30,8 +30,14 @@ __device__ __forceinline__ int tiles_of(int seq) {
 
 // Step a cursor to the next tile of the flattened (sequence, head group,
 // tile) list; past the end it reports n = 0.
+// seq_lens of sequence b, clamped: from the shared-memory copy made by the
+// prologue when the batch fits in it, else from global memory.
+__device__ __forceinline__ int seq_of(const DecodeParams& p, const int* sseq, int b, int cap) {
+  return b < kSeqCache ? sseq[b] : clamp_seq(__ldg(p.seq_lens + b), cap);
+}
+
 template <class TR>
-__device__ __forceinline__ void cursor_next(Cursor& c, const DecodeParams& p, int cap, int ngroups) {
+__device__ __forceinline__ void cursor_next(Cursor& c, const DecodeParams& p, int cap, int ngroups, const int* sseq) {
   if (++c.i < c.n) return;
   c.i = 0;
   c.pair_start += c.n;
@@ -42,13 +48,14 @@ __device__ __forceinline__ void cursor_next(Cursor& c, const DecodeParams& p, in
       c.n = 0;
       return;
     }
-    c.seq = clamp_seq(__ldg(p.seq_lens + c.b), cap);
+    c.seq = seq_of(p, sseq, c.b, cap);
     c.n = tiles_of<TR>(c.seq);
   } while (c.n == 0);
 }
 
 // Page ids of the TMA boxes of the tile at cursor `c`: lane l loads boxes
-// l, l + 32, ... Boxes past seq_len get id 0 and are never issued.
+// l, l + 32, ... Boxes past seq_len get id 0 and are never issued. The loads
+// are pinned in program order so that they start as early as written.
 template <class TR>
 __device__ __forceinline__ void load_page_ids(const DecodeParams& p, const Cursor& c, int lane,
                                               int (&dst)[TR::NB_PER_LANE]) {
@@ -58,7 +65,7 @@ __device__ __forceinline__ void load_page_ids(const DecodeParams& p, const Curso
   for (int u = 0; u < TR::NB_PER_LANE; ++u) {
     const int j = lane + 32 * u;
     const int tok = c.i * TR::TT + j * R;
-    dst[u] = (j * R < TR::TT && tok < c.seq) ? __ldg(p.block_table + row + tok / p.page_size) : 0;
+    dst[u] = (j * R < TR::TT && tok < c.seq) ? ld_nc_early(p.block_table + row + tok / p.page_size) : 0;
   }
 }
 
@@ -98,6 +105,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
   volatile int* abort_flag = scan + 12;
   int* cur_smem = scan + 16;                                         // Cursor as 6 ints
   int* sink = scan + 24;                                             // [consumer warps] scratch
+  int* sseq = scan + 64;                                             // [kSeqCache] clamped seq_lens
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int cap = p.max_pages * p.page_size;
@@ -106,6 +114,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
   const int G = p.gqa;
   const int ngroups = p.hkv / HG;
   if (tid == 0) PAD_STAMP(0);
+  if (tid == 32 * kConsumerWarps) {  // producer lane 0: descriptors of the three tensor maps
+    prefetch_tmap(&p.tm_k);
+    prefetch_tmap(&p.tm_v);
+    prefetch_tmap(&p.tm_q);
+  }
 
   // ---- set-up: zero the query tiles (rows past HG*G stay zero), init barriers
   for (int x = tid; x < TR::QSLOTS * TR::Q_BYTES / 16; x += kThreads)
@@ -148,11 +161,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
   // ---- block-wide exclusive scan of tiles per sequence (x head groups)
   const int per = (p.batch + kThreads - 1) / kThreads;
   const int b_lo = min(p.batch, tid * per), b_hi = min(p.batch, b_lo + per);
-  int local = 0, bad = 0;
+  int local = 0, bad = 0, any_empty = 0;
   for (int b = b_lo; b < b_hi; ++b) {
     const int raw = __ldg(p.seq_lens + b);
     bad |= (raw < 0 || raw > cap);
-    local += tiles_of<TR>(clamp_seq(raw, cap));
+    const int sq = clamp_seq(raw, cap);
+    if (b < kSeqCache) sseq[b] = sq;
+    any_empty |= (sq == 0);
+    local += tiles_of<TR>(sq);
   }
   local *= ngroups;
   int incl = local;
@@ -162,7 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     if (lane >= o) incl += y;
   }
   if (lane == 31) scan[warp] = incl;
-  __syncthreads();
+  any_empty = __syncthreads_or(any_empty);
   int excl = incl - local, total = 0;
   for (int x = 0; x < kThreads / 32; ++x) {
     const int v = scan[x];
@@ -175,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
   if (t0 < total && excl <= t0 && t0 < excl + local) {
     int acc_t = excl;
     for (int b = b_lo; b < b_hi; ++b) {
-      const int seq = clamp_seq(__ldg(p.seq_lens + b), cap);
+      const int seq = seq_of(p, sseq, b, cap);
       const int n = tiles_of<TR>(seq);
       const int tb = n * ngroups;
       if (t0 < acc_t + tb) {
@@ -198,8 +214,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
   if (tid == 0) pdl_launch_dependents();
 
   // ---- zero output rows of empty sequences (src/reference.py:32-34)
-  for (int b = w; b < p.batch; b += (int)W) {
-    if (clamp_seq(__ldg(p.seq_lens + b), cap) == 0) {
+  // (only when the scan saw one: no extra global reads on the common path)
+  for (int b = w; any_empty && b < p.batch; b += (int)W) {
+    if (seq_of(p, sseq, b, cap) == 0) {
+      if (p.meta_by_pair && tid < ngroups) p.ws_meta[b * ngroups + tid] = make_int4(-1, 0, 0, 0);
       const int hq = p.hkv * G;
       for (int x = tid; x < hq * (D / 2); x += kThreads) {
         const int hh = x / (D / 2), d = (x % (D / 2)) * 2;
@@ -212,7 +230,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
 
   if (warp == kConsumerWarps) {
     // =============================== producer warp ===============================
-    if (lane == 0) p.ws_meta[w] = make_int4(-1, 0, 0, 0);
+    if (lane == 0 && !p.meta_by_pair) p.ws_meta[w] = make_int4(-1, 0, 0, 0);
+    if (lane == 0) PAD_STAMP(7);
     if (ntiles <= 0) {
       // An empty partition (more partitions than tiles) can sit between the
       // first and last partition of a split pair; it owns a partial slot of
@@ -224,6 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
       return;
     }
     const int R = p.box_rows;
+    const uint64_t kv_policy = l2_evict_first_policy();
     Cursor c{cur_smem[0], cur_smem[1], cur_smem[2], cur_smem[3], cur_smem[4], cur_smem[5]};
     Cursor la = c;
     int pid[S][TR::NB_PER_LANE];
@@ -241,9 +261,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
         } else {
           load_page_ids<TR>(p, la, lane, pid[k]);
         }
-        cursor_next<TR>(la, p, cap, ngroups);
+        cursor_next<TR>(la, p, cap, ngroups, sseq);
       }
     }
+    if (lane == 0) PAD_STAMP(5);
 #pragma unroll
     for (int k = 0; k < S; ++k)
       if (k < ntiles) store_page_ids<TR>(ids + k * TR::NB_MAX, lane, pid[k]);
@@ -278,6 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
         if (segs >= TR::QSLOTS) ok = mbar_wait_bounded(&qempty[qs], ((segs / TR::QSLOTS) - 1) & 1, kWaitTimeoutNs);
         if (!__all_sync(0xffffffffu, ok)) break;
         if (lane == 0) {
+          if (k == 0) PAD_STAMP(6);
           mbar_arrive_expect_tx(&qfull[qs], qbytes);
 #pragma unroll
           for (int sg = 0; sg < TR::NSEG; ++sg)
@@ -299,9 +321,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
         dsc.qslot = qs;
         dsc.pad = 0;
         descs[s] = dsc;
-        if (split && c.i == 0) {
+        // The partition holding a pair's first tile publishes its merge
+        // descriptor (indexed by pair or by partition, see meta_by_pair).
+        if (c.i == 0 && (split || p.meta_by_pair)) {
           const int last_owner = part_owner((int64_t)c.pair_start + c.n - 1, total, W);
-          p.ws_meta[w] = make_int4(pair, pair + w, last_owner - w + 1, 1);
+          p.ws_meta[p.meta_by_pair ? pair : w] =
+              split ? make_int4(pair, pair + w, last_owner - w + 1, 1) : make_int4(-1, 0, 0, 0);
         }
         mbar_arrive_expect_tx(&full[s], (uint32_t)nvalid * R * HG * TR::ROW_BYTES * 2);
       }
@@ -314,8 +339,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
 #pragma unroll
         for (int sg = 0; sg < TR::NSEG; ++sg) {
           const int off = sg * kTileRows * TR::SEGW + j * (int)TR::box_pitch(R);
-          tma_load_4d(st + off, &p.tm_k, &full[s], sg * (TR::SEGW / 2), row, c.hg * HG, page);
-          tma_load_4d(st + TR::KT_BYTES + off, &p.tm_v, &full[s], sg * (TR::SEGW / 2), row, c.hg * HG, page);
+          tma_load_4d_hint(st + off, &p.tm_k, &full[s], sg * (TR::SEGW / 2), row, c.hg * HG, page, kv_policy);
+          tma_load_4d_hint(st + TR::KT_BYTES + off, &p.tm_v, &full[s], sg * (TR::SEGW / 2), row, c.hg * HG, page,
+                           kv_policy);
         }
       }
       if (k == 0 && lane == 0) PAD_STAMP(2);
@@ -323,10 +349,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
       if (first) ++segs;
       if (k + S < ntiles) {
         load_page_ids<TR>(p, la, lane, pend);
-        cursor_next<TR>(la, p, cap, ngroups);
+        cursor_next<TR>(la, p, cap, ngroups, sseq);
         have_pend = true;
       }
-      cursor_next<TR>(c, p, cap, ngroups);
+      cursor_next<TR>(c, p, cap, ngroups, sseq);
     }
     if (!ok) {
       // Unwind: record the failure, stop the consumers, and wait (bounded)
@@ -490,7 +516,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     if (lane == 0) mbar_arrive(&empty[s]);
 
     if (dsc.flags & kLast) {
-      if (warp == 0 && lane == 0) PAD_STAMP(6);
       // ------------- segment epilogue: merge the WPH warps of each head, write
       // the fp16 output rows (pair finished here) or the fp32 partial (split pair)
       float lsum[NT][2];
@@ -575,7 +600,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
           }
           consumer_sync();
         }
-        if (warp == 0 && lane == 0) PAD_STAMP(7);
         const int ctid = warp * 32 + lane;
         if (!split) {
           __half* obase = p.out + dsc.b * p.out_sb + (int64_t)(dsc.hg * HG * G) * p.out_sh;
@@ -602,12 +626,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
       }
     }
   }
-  if (warp == 0 && lane == 0) PAD_STAMP(5);
 }
 
 // Phase 2: merge the partials of one split (sequence, head group) pair for
 // one (head, query row). Grid (partitions, HG*G); partition w works only if
-// it is the first partition of a split pair (ws_meta[w].w == 1).
+// it is the first partition of a split pair (ws_meta[w].w == 1); when there
+// are fewer pairs than partitions the grid and descriptors go by pair instead.
 //   M = max_s m_s;  L = sum_s l_s 2^(m_s - M);  O = sum_s O_s 2^(m_s - M) / L
 // (analysis/split_k_derivation.md:44-65; a partial with m_s = -inf weighs 0
 // and its O is not read, the guard of analysis/split_k_derivation.md:67-86).
@@ -615,15 +639,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
 // (loads issued four at a time), then the per-thread states are combined
 // through shared memory. Launched as a programmatic dependent of the decode
 // kernel: it waits on griddepcontrol before reading the partials.
-template <int D, int kMergeThreads>
+template <int D, int kMergeThreads, int DS>
 __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const float* __restrict__ ws_o,
                                                               const float2* __restrict__ ws_ml,
                                                               const int4* __restrict__ ws_meta,
                                                               __half* __restrict__ out, int64_t out_sb,
                                                               int64_t out_sh, int ngroups, int rows) {
-  constexpr int C4 = D / 4;                // float4 columns of one partial row
+  constexpr int DC = D / DS;               // columns of D this CTA merges (blockIdx.z picks which)
+  constexpr int C4 = DC / 4;               // float4 columns of one partial row slice
   constexpr int PG = kMergeThreads / C4;   // partial groups folded in parallel
-  __shared__ float red_o[PG][D];
+  __shared__ float red_o[PG][DC];
   __shared__ float red_m[PG], red_l[PG];
   pdl_wait_primary();
   const int w = blockIdx.x, y = blockIdx.y, tid = threadIdx.x;
@@ -631,7 +656,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const float* __res
   const int4 meta = ws_meta[w];
   if (meta.w != 1) return;
   const int pair = meta.x, s0 = meta.y, ns = meta.z;
-  const int c = tid % C4, sg = tid / C4;
+  const int c = tid % C4 + blockIdx.z * C4, sg = tid / C4;
   float m = -INFINITY, l = 0.f;
   float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int s = sg; s < ns; s += 4 * PG) {
@@ -660,8 +685,8 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const float* __res
       m = mn;
     }
   }
-  *reinterpret_cast<float4*>(&red_o[sg][c * 4]) = a;
-  if (c == 0) {
+  *reinterpret_cast<float4*>(&red_o[sg][(c - blockIdx.z * C4) * 4]) = a;
+  if (tid % C4 == 0) {
     red_m[sg] = m;
     red_l[sg] = l;
   }
@@ -685,7 +710,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const float* __res
     }
     const float inv = L > 0.f ? 1.f / L : 0.f;
     const int b = pair / ngroups, hg = pair % ngroups;
-    __half* o = out + b * out_sb + (int64_t)(hg * rows + y) * out_sh + tid * 4;
+    __half* o = out + b * out_sb + (int64_t)(hg * rows + y) * out_sh + blockIdx.z * DC + tid * 4;
     reinterpret_cast<__half2*>(o)[0] = __floats2half2_rn(t.x * inv, t.y * inv);
     reinterpret_cast<__half2*>(o)[1] = __floats2half2_rn(t.z * inv, t.w * inv);
     if (tid == 0) PAD_STAMP_MAX(1);

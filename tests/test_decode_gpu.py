@@ -238,3 +238,15 @@ def test_head_group_page_split_matrix(hkv, head_dim, page_size):
     ref = oracle.decode_c(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens)
     for s in (None, 1, 2, 3, 4, 5, 6, 7, 9):
         assert_parity(run(c, num_splits=s), ref, f"hkv={hkv} D={head_dim} ps={page_size} S={s}")
+
+
+def test_reused_workspace_split_then_empty_pair():
+    """Merge descriptors live in the reused workspace: a pair split in one call
+    and empty (seq_len 0) in the next must not be merged from stale partials."""
+    a = explicit_case([8000, 9000], num_kv_heads=2, gqa_ratio=6, head_dim=128, page_size=16, seed=31)
+    run(a)  # both pairs split across many partitions
+    b = explicit_case([0, 9000], num_kv_heads=2, gqa_ratio=6, head_dim=128, page_size=16, seed=32)
+    out = run(b)
+    assert np.all(out[0] == 0)
+    ref = oracle.decode_c(b.q, b.k_cache, b.v_cache, b.block_table, b.seq_lens)
+    assert_parity(out, ref)
