@@ -114,6 +114,28 @@ int pad_paged_attention_decode(const void* q, const void* k_cache, const void* v
                                int64_t num_splits, void* workspace, size_t workspace_bytes,
                                void* stream, int32_t* error_flags);
 
+/* Decode with a CSR page index instead of a dense block table -- the
+ * (indptr, indices, last_page_len) layout the reference's FlashInfer adapter
+ * builds from a block table (src/flashinfer_adapter.py:40-65):
+ *   pages of sequence b = kv_indices[kv_indptr[b] .. kv_indptr[b+1])
+ *   seq_len of b        = (pages - 1) * page_size + kv_last_page_len[b]
+ *                         (0 when the sequence has no pages)
+ * nnz_pages is the length of kv_indices. Everything else -- strides, scale,
+ * num_splits, workspace (sized by pad_decode_csr_workspace_bytes), stream,
+ * error flags -- is as for pad_paged_attention_decode. */
+int pad_decode_csr_workspace_bytes(int device, int64_t batch, int64_t num_kv_heads, int64_t gqa_ratio,
+                                   int64_t head_dim, int64_t page_size, int64_t nnz_pages,
+                                   int64_t num_splits, size_t* bytes);
+int pad_paged_attention_decode_csr(const void* q, const void* k_cache, const void* v_cache,
+                                   const int32_t* kv_indptr, const int32_t* kv_indices,
+                                   const int32_t* kv_last_page_len, void* out, int64_t batch,
+                                   int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
+                                   int64_t num_pages, int64_t page_size, int64_t nnz_pages,
+                                   const int64_t* q_strides, const int64_t* k_strides,
+                                   const int64_t* v_strides, const int64_t* out_strides, float scale,
+                                   int64_t num_splits, void* workspace, size_t workspace_bytes,
+                                   void* stream, int32_t* error_flags);
+
 /* Decode without any device allocation, for callers that cannot call
  * cudaMalloc: code running inside a CUDA stream capture they do not own,
  * embedders whose memory is owned by a custom allocator or a fixed arena,

@@ -169,8 +169,10 @@ struct Plan {
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// max_pages: block-table width (dense) or total pages of the index (CSR,
+// csr = true), which bounds the tiles differently.
 int make_plan(int device, int64_t batch, int64_t hkv, int64_t gqa, int64_t head_dim, int64_t page_size,
-              int64_t max_pages, int64_t num_splits, Plan* plan) {
+              int64_t max_pages, int64_t num_splits, Plan* plan, bool csr = false) {
   if (batch < 0 || hkv <= 0 || gqa <= 0 || page_size <= 0 || max_pages < 0)
     return fail(PAD_ERR_INVALID_ARGUMENT,
                 "invalid sizes: batch=%lld num_kv_heads=%lld gqa_ratio=%lld page_size=%lld max_pages=%lld",
@@ -183,7 +185,7 @@ int make_plan(int device, int64_t batch, int64_t hkv, int64_t gqa, int64_t head_
   const int tt = kTileRows / hg;
   const int64_t tiles_max = (cap + tt - 1) / tt;
   const int64_t groups = hkv / hg;
-  const int64_t tiles_ub = batch * groups * tiles_max;
+  const int64_t tiles_ub = csr ? groups * (tiles_max + batch) : batch * groups * tiles_max;
   if (cap > INT32_MAX || tiles_ub > INT32_MAX / 2 || batch * groups > INT32_MAX / 4)
     return fail(PAD_ERR_UNSUPPORTED, "problem too large for 32-bit tile indexing (%lld tiles)", (long long)tiles_ub);
   plan->box_rows = box_rows_for(page_size, tt);
@@ -293,13 +295,20 @@ int pad_decode_workspace_bytes(int device, int64_t batch, int64_t num_kv_heads, 
   return st;
 }
 
-int pad_paged_attention_decode(const void* q, const void* k_cache, const void* v_cache, const int32_t* block_table,
-                               const int32_t* seq_lens, void* out, int64_t batch, int64_t num_q_heads,
-                               int64_t num_kv_heads, int64_t head_dim, int64_t num_pages, int64_t page_size,
-                               int64_t max_pages_per_seq, const int64_t* q_strides, const int64_t* k_strides,
-                               const int64_t* v_strides, int64_t block_table_stride, const int64_t* out_strides,
-                               float scale, int64_t num_splits, void* workspace, size_t workspace_bytes, void* stream,
-                               int32_t* error_flags) {
+}  // extern "C"
+
+namespace {
+
+// Shared body of the dense and the CSR entry points (csr_indptr == nullptr:
+// dense block table + seq_lens; else block_table is the CSR `indices` array
+// of max_pages_per_seq = nnz entries).
+int decode_impl(const void* q, const void* k_cache, const void* v_cache, const int32_t* block_table,
+                const int32_t* seq_lens, const int32_t* csr_indptr, const int32_t* csr_last, void* out, int64_t batch,
+                int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t num_pages, int64_t page_size,
+                int64_t max_pages_per_seq, const int64_t* q_strides, const int64_t* k_strides,
+                const int64_t* v_strides, int64_t block_table_stride, const int64_t* out_strides, float scale,
+                int64_t num_splits, void* workspace, size_t workspace_bytes, void* stream, int32_t* error_flags) {
+  const bool csr = csr_indptr != nullptr;
   // ---- shape-only checks (no device access, no sync)
   if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || num_pages < 0 || page_size <= 0 ||
       max_pages_per_seq < 0)
@@ -312,8 +321,8 @@ int pad_paged_attention_decode(const void* q, const void* k_cache, const void* v
   if (!std::isfinite(scale)) return fail(PAD_ERR_INVALID_ARGUMENT, "scale must be finite");
   const int64_t gqa = num_q_heads / num_kv_heads;
   if (batch == 0) return PAD_OK;
-  if (q == nullptr || k_cache == nullptr || v_cache == nullptr || block_table == nullptr || seq_lens == nullptr ||
-      out == nullptr)
+  if (q == nullptr || k_cache == nullptr || v_cache == nullptr || block_table == nullptr ||
+      (!csr && seq_lens == nullptr) || (csr && csr_last == nullptr) || out == nullptr)
     return fail(PAD_ERR_INVALID_ARGUMENT, "null tensor pointer");
   if (q_strides[2] != 1 || k_strides[3] != 1 || v_strides[3] != 1 || out_strides[2] != 1)
     return fail(PAD_ERR_UNSUPPORTED, "the head_dim axis of q, k_cache, v_cache and out must be contiguous");
@@ -326,7 +335,7 @@ int pad_paged_attention_decode(const void* q, const void* k_cache, const void* v
     return fail(PAD_ERR_UNSUPPORTED, "out strides must be even");
   if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out))
     return fail(PAD_ERR_UNSUPPORTED, "q, k_cache, v_cache and out must be 16-byte aligned");
-  if (max_pages_per_seq > 0 && block_table_stride < max_pages_per_seq)
+  if (!csr && max_pages_per_seq > 0 && block_table_stride < max_pages_per_seq)
     return fail(PAD_ERR_INVALID_ARGUMENT, "block_table row stride smaller than its width");
   if (num_pages == 0 || max_pages_per_seq == 0) {
     // Nothing addressable: every sequence must be empty. Zero the output.
@@ -344,7 +353,7 @@ int pad_paged_attention_decode(const void* q, const void* k_cache, const void* v
   cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   Plan plan;
-  int st = make_plan(device, batch, num_kv_heads, gqa, head_dim, page_size, max_pages_per_seq, num_splits, &plan);
+  int st = make_plan(device, batch, num_kv_heads, gqa, head_dim, page_size, max_pages_per_seq, num_splits, &plan, csr);
   if (st != PAD_OK) return st;
   if (workspace == nullptr || workspace_bytes < plan.bytes)
     return fail(PAD_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", plan.bytes,
@@ -377,6 +386,8 @@ int pad_paged_attention_decode(const void* q, const void* k_cache, const void* v
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   prm.block_table = block_table;
   prm.seq_lens = seq_lens;
+  prm.csr_indptr = csr_indptr;
+  prm.csr_last = csr_last;
   prm.out = static_cast<__half*>(out);
   prm.ws_meta = reinterpret_cast<int4*>(ws + plan.off_meta);
   prm.ws_ml = reinterpret_cast<float2*>(ws + plan.off_ml);
@@ -424,6 +435,46 @@ int pad_paged_attention_decode(const void* q, const void* k_cache, const void* v
     if (e != cudaSuccess) return cuda_fail(e, "launching the merge kernel");
   }
   return PAD_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int pad_paged_attention_decode(const void* q, const void* k_cache, const void* v_cache, const int32_t* block_table,
+                               const int32_t* seq_lens, void* out, int64_t batch, int64_t num_q_heads,
+                               int64_t num_kv_heads, int64_t head_dim, int64_t num_pages, int64_t page_size,
+                               int64_t max_pages_per_seq, const int64_t* q_strides, const int64_t* k_strides,
+                               const int64_t* v_strides, int64_t block_table_stride, const int64_t* out_strides,
+                               float scale, int64_t num_splits, void* workspace, size_t workspace_bytes, void* stream,
+                               int32_t* error_flags) {
+  return decode_impl(q, k_cache, v_cache, block_table, seq_lens, nullptr, nullptr, out, batch, num_q_heads,
+                     num_kv_heads, head_dim, num_pages, page_size, max_pages_per_seq, q_strides, k_strides, v_strides,
+                     block_table_stride, out_strides, scale, num_splits, workspace, workspace_bytes, stream,
+                     error_flags);
+}
+
+int pad_decode_csr_workspace_bytes(int device, int64_t batch, int64_t num_kv_heads, int64_t gqa_ratio,
+                                   int64_t head_dim, int64_t page_size, int64_t nnz_pages, int64_t num_splits,
+                                   size_t* bytes) {
+  if (bytes == nullptr) return fail(PAD_ERR_INVALID_ARGUMENT, "null output pointer");
+  Plan plan;
+  int st = make_plan(device, batch, num_kv_heads, gqa_ratio, head_dim, page_size, nnz_pages, num_splits, &plan, true);
+  if (st == PAD_OK) *bytes = plan.bytes;
+  return st;
+}
+
+int pad_paged_attention_decode_csr(const void* q, const void* k_cache, const void* v_cache, const int32_t* kv_indptr,
+                                   const int32_t* kv_indices, const int32_t* kv_last_page_len, void* out,
+                                   int64_t batch, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
+                                   int64_t num_pages, int64_t page_size, int64_t nnz_pages,
+                                   const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                                   const int64_t* out_strides, float scale, int64_t num_splits, void* workspace,
+                                   size_t workspace_bytes, void* stream, int32_t* error_flags) {
+  if (kv_indptr == nullptr && batch > 0) return fail(PAD_ERR_INVALID_ARGUMENT, "null kv_indptr");
+  return decode_impl(q, k_cache, v_cache, kv_indices, nullptr, kv_indptr, kv_last_page_len, out, batch, num_q_heads,
+                     num_kv_heads, head_dim, num_pages, page_size, nnz_pages, q_strides, k_strides, v_strides,
+                     nnz_pages, out_strides, scale, num_splits, workspace, workspace_bytes, stream, error_flags);
 }
 
 // ----------------------------------------------------------------- no-alloc entry

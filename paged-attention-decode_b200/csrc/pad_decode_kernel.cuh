@@ -51,6 +51,11 @@ struct __align__(64) DecodeParams {
   int4* ws_meta;    // [partitions] merge descriptors {pair, first slot, n slots, valid}
   int32_t* error_flags;
   int64_t bt_stride;
+  // CSR page index (FlashInfer layout): when csr_indptr is set, sequence b's
+  // pages are block_table[csr_indptr[b] .. csr_indptr[b+1]) (block_table is the
+  // flat `indices` array) and seq_len = (pages - 1) * page_size + csr_last[b].
+  const int32_t* csr_indptr;
+  const int32_t* csr_last;
   int64_t out_sb, out_sh;
   int batch, hkv, gqa, page_size, num_pages, max_pages;
   int box_rows;      // R: tokens per TMA box (divides page_size and TT)
@@ -138,6 +143,7 @@ constexpr int kFirst = 1, kLast = 2, kSplit = 4;
 struct Cursor {
   int b, hg, i, n, seq;  // n = tiles of sequence b
   int pair_start;        // global index of tile 0 of pair (b, hg)
+  int64_t base;          // offset of sequence b's row in the page index
 };
 
 __device__ __forceinline__ int clamp_seq(int raw, int cap) { return raw < 0 ? 0 : (raw > cap ? cap : raw); }

@@ -32,8 +32,21 @@ __device__ __forceinline__ int tiles_of(int seq) {
 // tile) list; past the end it reports n = 0.
 // seq_lens of sequence b, clamped: from the shared-memory copy made by the
 // prologue when the batch fits in it, else from global memory.
+// seq_len of sequence b as given (dense: seq_lens[b]; CSR: from the page
+// count and the last page's fill).
+__device__ __forceinline__ int raw_seq(const DecodeParams& p, int b) {
+  if (p.csr_indptr == nullptr) return __ldg(p.seq_lens + b);
+  const int pages = __ldg(p.csr_indptr + b + 1) - __ldg(p.csr_indptr + b);
+  return pages > 0 ? (pages - 1) * p.page_size + __ldg(p.csr_last + b) : 0;
+}
+
+// Offset of sequence b's row of page ids.
+__device__ __forceinline__ int64_t row_base(const DecodeParams& p, int b) {
+  return p.csr_indptr == nullptr ? (int64_t)b * p.bt_stride : (int64_t)__ldg(p.csr_indptr + b);
+}
+
 __device__ __forceinline__ int seq_of(const DecodeParams& p, const int* sseq, int b, int cap) {
-  return b < kSeqCache ? sseq[b] : clamp_seq(__ldg(p.seq_lens + b), cap);
+  return b < kSeqCache ? sseq[b] : clamp_seq(raw_seq(p, b), cap);
 }
 
 template <class TR>
@@ -50,6 +63,7 @@ __device__ __forceinline__ void cursor_next(Cursor& c, const DecodeParams& p, in
     }
     c.seq = seq_of(p, sseq, c.b, cap);
     c.n = tiles_of<TR>(c.seq);
+    c.base = row_base(p, c.b);
   } while (c.n == 0);
 }
 
@@ -60,7 +74,7 @@ template <class TR>
 __device__ __forceinline__ void load_page_ids(const DecodeParams& p, const Cursor& c, int lane,
                                               int (&dst)[TR::NB_PER_LANE]) {
   const int R = p.box_rows;
-  const int64_t row = (int64_t)c.b * p.bt_stride;
+  const int64_t row = c.base;
 #pragma unroll
   for (int u = 0; u < TR::NB_PER_LANE; ++u) {
     const int j = lane + 32 * u;
@@ -142,7 +156,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
   // every sequence fills its block-table row (true for uniform batches) and
   // loads their page ids now, overlapping the seq_lens round trip below.
   const int ncap = tiles_of<TR>(cap);
-  const int64_t tg_total = (int64_t)p.batch * ngroups * ncap;
+  // (no guess for a CSR index: its rows have no fixed width)
+  const int64_t tg_total = p.csr_indptr == nullptr ? (int64_t)p.batch * ngroups * ncap : 0;
   const int tg0 = tg_total > 0 ? part_begin(w, tg_total, W) : 0;
   int gpid[S][TR::NB_PER_LANE];
   if (warp == kConsumerWarps) {
@@ -152,7 +167,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
       if (t < tg_total) {
         const int per_seq = ngroups * ncap;
         const int r = (int)(t % per_seq);
-        const Cursor gc{(int)(t / per_seq), r / ncap, r % ncap, ncap, cap, 0};
+        const Cursor gc{(int)(t / per_seq), r / ncap, r % ncap, ncap, cap, 0, (t / per_seq) * p.bt_stride};
         load_page_ids<TR>(p, gc, lane, gpid[k]);
       }
     }
@@ -163,7 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
   const int b_lo = min(p.batch, tid * per), b_hi = min(p.batch, b_lo + per);
   int local = 0, bad = 0, any_empty = 0;
   for (int b = b_lo; b < b_hi; ++b) {
-    const int raw = __ldg(p.seq_lens + b);
+    const int raw = raw_seq(p, b);
     bad |= (raw < 0 || raw > cap);
     const int sq = clamp_seq(raw, cap);
     if (b < kSeqCache) sseq[b] = sq;
@@ -244,7 +259,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     }
     const int R = p.box_rows;
     const uint64_t kv_policy = l2_evict_first_policy();
-    Cursor c{cur_smem[0], cur_smem[1], cur_smem[2], cur_smem[3], cur_smem[4], cur_smem[5]};
+    Cursor c{cur_smem[0], cur_smem[1], cur_smem[2], cur_smem[3], cur_smem[4], cur_smem[5], 0};
+    c.base = row_base(p, c.b);
     Cursor la = c;
     int pid[S][TR::NB_PER_LANE];
     const int per_seq = ngroups * ncap;

@@ -39,6 +39,10 @@ SIGNATURES = {
     "pad_paged_attention_decode": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp] + [_c_i64] * 7
                                    + [_c_i64p, _c_i64p, _c_i64p, _c_i64, _c_i64p, ctypes.c_float, _c_i64,
                                       _vp, ctypes.c_size_t, _vp, _vp]),
+    "pad_decode_csr_workspace_bytes": (ctypes.c_int, [ctypes.c_int] + [_c_i64] * 7 + [ctypes.POINTER(ctypes.c_size_t)]),
+    "pad_paged_attention_decode_csr": (ctypes.c_int, [_vp] * 7 + [_c_i64] * 7
+                                       + [_c_i64p, _c_i64p, _c_i64p, _c_i64p, ctypes.c_float, _c_i64, _vp,
+                                          ctypes.c_size_t, _vp, _vp]),
     "pad_paged_attention_decode_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp] + [_c_i64] * 7
                                            + [_c_i64p, _c_i64p, _c_i64p, _c_i64, _c_i64p, ctypes.c_float,
                                               _c_i64, _vp, _vp]),

@@ -172,3 +172,80 @@ def read_error_flags(device: torch.device | None = None, reset: bool = True) -> 
     if reset:
         st.flags.zero_()
     return v
+
+
+def paged_kv_indices(block_table: torch.Tensor, seq_lens: torch.Tensor, page_size: int):
+    """Dense block table + seq_lens -> CSR (indptr, indices, last_page_len).
+
+    The conversion of the reference's FlashInfer adapter
+    (src/flashinfer_adapter.py:40-65): sequence b uses its first
+    ceil(seq_len/page_size) block-table entries; last_page_len lies in
+    [1, page_size] (page_size for an empty sequence, which has no pages)."""
+    sl = seq_lens.to(torch.int64)
+    pages = (sl + page_size - 1) // page_size
+    mask = torch.arange(block_table.shape[1], device=block_table.device)[None, :] < pages[:, None]
+    indices = block_table[mask].to(torch.int32)
+    indptr = torch.zeros(block_table.shape[0] + 1, dtype=torch.int32, device=block_table.device)
+    indptr[1:] = torch.cumsum(pages, 0).to(torch.int32)
+    last = (sl - (pages - 1) * page_size).to(torch.int32)
+    return indptr, indices, last
+
+
+def paged_attention_decode_csr(
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    kv_indptr: torch.Tensor,
+    kv_indices: torch.Tensor,
+    kv_last_page_len: torch.Tensor,
+    num_splits: int | None = None,
+    scale: float | None = None,
+    *,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Decode over a paged fp16 KV cache addressed by a CSR page index
+    (kv_indptr [B+1], kv_indices [nnz], kv_last_page_len [B], int32) --
+    the format of the reference's FlashInfer comparison path -- on the same
+    B200 kernel as paged_attention_decode_cuda_v4."""
+    assert q.is_cuda and k_cache.is_cuda and v_cache.is_cuda, "pad_b200 requires CUDA tensors"
+    assert q.dtype == torch.float16 and k_cache.dtype == torch.float16 and v_cache.dtype == torch.float16, (
+        "pad_b200 expects fp16 q/k_cache/v_cache"
+    )
+    batch, num_q_heads, head_dim = q.shape
+    num_pages, page_size, num_kv_heads, _ = k_cache.shape
+    assert v_cache.shape == k_cache.shape and k_cache.shape[3] == head_dim
+    assert num_q_heads % num_kv_heads == 0, "num_q_heads must be divisible by num_kv_heads (GQA)"
+    assert head_dim in _SUPPORTED_HEAD_DIMS, f"head_dim must be one of {_SUPPORTED_HEAD_DIMS}"
+    assert kv_indptr.shape == (batch + 1,) and kv_last_page_len.shape == (batch,), "bad CSR shapes"
+    dev = q.device
+    indptr = kv_indptr.to(device=dev, dtype=torch.int32).contiguous()
+    indices = kv_indices.to(device=dev, dtype=torch.int32).contiguous()
+    last = kv_last_page_len.to(device=dev, dtype=torch.int32).contiguous()
+    scale = scale if scale is not None else 1.0 / math.sqrt(head_dim)
+    if q.stride(2) != 1 or q.stride(0) % 8 or q.stride(1) % 8 or q.data_ptr() % 16:
+        q = q.contiguous()
+    if out is None:
+        out = torch.empty((batch, num_q_heads, head_dim), dtype=torch.float16, device=dev)
+    if batch == 0:
+        return out
+    nnz = max(int(indices.numel()), 1)
+    if indices.numel() == 0:
+        indices = torch.zeros(1, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        st = _state(dev, stream)
+        splits = 0 if num_splits is None else int(num_splits)
+        lib = _lib.load()
+        need = _lib.ctypes.c_size_t(0)
+        _lib.check(lib.pad_decode_csr_workspace_bytes(dev.index, batch, num_kv_heads, num_q_heads // num_kv_heads,
+                                                      head_dim, page_size, nnz, splits, _lib.ctypes.byref(need)))
+        ws = st.workspace_ptr(int(need.value))
+        _lib.check(lib.pad_paged_attention_decode_csr(
+            q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), indptr.data_ptr(), indices.data_ptr(),
+            last.data_ptr(), out.data_ptr(), batch, num_q_heads, num_kv_heads, head_dim, num_pages, page_size, nnz,
+            _lib.i64_array(q.stride()), _lib.i64_array(k_cache.stride()), _lib.i64_array(v_cache.stride()),
+            _lib.i64_array(out.stride()), float(scale), splits, ws, st.workspace.numel(), stream,
+            st.flags.data_ptr()))
+        if _CHECK_VALUES:
+            _raise_for_flags(int(st.flags.item()))
+    return out
