@@ -136,6 +136,22 @@ int pad_paged_attention_decode_csr(const void* q, const void* k_cache, const voi
                                    int64_t num_splits, void* workspace, size_t workspace_bytes,
                                    void* stream, int32_t* error_flags);
 
+/* Write one new token's K and V per sequence into the paged cache (the step
+ * before decode; the reference fixes this cache layout, README.md:38-44, but
+ * has no writer). Token positions[b] of sequence b goes to page
+ * block_table[b, positions[b] / page_size], row positions[b] % page_size,
+ * for every KV head; positions[b] < 0 skips sequence b.
+ * k_new / v_new are [batch, num_kv_heads, head_dim] fp16 with strides
+ * k_new_strides[3] / v_new_strides[3]; caches as for decode. A position past
+ * the block table sets PAD_FLAG_SEQ_LEN_RANGE, a bad page id
+ * PAD_FLAG_BAD_PAGE_ID (nothing is written for that row). */
+int pad_paged_kv_append(const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                        const int32_t* block_table, const int32_t* positions, int64_t batch,
+                        int64_t num_kv_heads, int64_t head_dim, int64_t num_pages, int64_t page_size,
+                        int64_t max_pages_per_seq, const int64_t* k_new_strides,
+                        const int64_t* v_new_strides, const int64_t* k_strides, const int64_t* v_strides,
+                        int64_t block_table_stride, void* stream, int32_t* error_flags);
+
 /* Decode without any device allocation, for callers that cannot call
  * cudaMalloc: code running inside a CUDA stream capture they do not own,
  * embedders whose memory is owned by a custom allocator or a fixed arena,

@@ -10,7 +10,7 @@ The public call is the reference project's wrapper signature
 backed by the C-ABI library libpad_b200.so (include/pad_b200.h).
 """
 
-from .kernel_cuda_v4 import (paged_attention_decode_csr, paged_attention_decode_cuda_v4, paged_kv_indices,  # noqa: F401
+from .kernel_cuda_v4 import (paged_attention_decode_csr, paged_attention_decode_cuda_v4, paged_kv_append, paged_kv_indices,  # noqa: F401
                              partitions, read_error_flags, workspace_bytes)
 from ._lib import PadError  # noqa: F401
 
@@ -24,5 +24,5 @@ def paged_attention_decode_v4(q, k_cache, v_cache, block_table, seq_lens, num_sp
 
 
 __all__ = ["paged_attention_decode_cuda_v4", "paged_attention_decode_v4", "paged_attention_decode_csr",
-           "paged_kv_indices", "partitions", "workspace_bytes",
+           "paged_kv_indices", "paged_kv_append", "partitions", "workspace_bytes",
            "read_error_flags", "PadError"]

@@ -43,6 +43,7 @@ SIGNATURES = {
     "pad_paged_attention_decode_csr": (ctypes.c_int, [_vp] * 7 + [_c_i64] * 7
                                        + [_c_i64p, _c_i64p, _c_i64p, _c_i64p, ctypes.c_float, _c_i64, _vp,
                                           ctypes.c_size_t, _vp, _vp]),
+    "pad_paged_kv_append": (ctypes.c_int, [_vp] * 6 + [_c_i64] * 6 + [_c_i64p] * 4 + [_c_i64, _vp, _vp]),
     "pad_paged_attention_decode_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp] + [_c_i64] * 7
                                            + [_c_i64p, _c_i64p, _c_i64p, _c_i64, _c_i64p, ctypes.c_float,
                                               _c_i64, _vp, _vp]),

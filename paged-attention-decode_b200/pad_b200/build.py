@@ -20,7 +20,7 @@ CSRC = os.path.join(PKG_ROOT, "csrc")
 INCLUDE = os.path.join(REPO, "include")
 LIB_NAME = "libpad_b200.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
-SOURCES = ["pad_decode.cu"]
+SOURCES = ["pad_decode.cu", "pad_kv_append.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -249,3 +249,31 @@ def paged_attention_decode_csr(
         if _CHECK_VALUES:
             _raise_for_flags(int(st.flags.item()))
     return out
+
+
+def paged_kv_append(k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                    block_table: torch.Tensor, positions: torch.Tensor) -> None:
+    """Write token positions[b] (k_new/v_new [B, Hkv, D] fp16) of every
+    sequence into the paged caches in place; positions[b] < 0 skips b."""
+    assert k_new.is_cuda and k_cache.is_cuda and k_new.dtype == torch.float16 and k_cache.dtype == torch.float16
+    assert v_new.shape == k_new.shape and v_cache.shape == k_cache.shape
+    batch, hkv, d = k_new.shape
+    num_pages, page_size, cache_hkv, cache_d = k_cache.shape
+    assert (cache_hkv, cache_d) == (hkv, d), "k_new must be [B, Hkv, D] matching the cache"
+    dev = k_cache.device
+    bt = block_table.to(device=dev, dtype=torch.int32)
+    if bt.stride(1) != 1:
+        bt = bt.contiguous()
+    pos = positions.to(device=dev, dtype=torch.int32).contiguous()
+    k_new = k_new if k_new.stride(2) == 1 else k_new.contiguous()
+    v_new = v_new if v_new.stride(2) == 1 else v_new.contiguous()
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        st = _state(dev, stream)
+        _lib.check(_lib.load().pad_paged_kv_append(
+            k_new.data_ptr(), v_new.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), bt.data_ptr(), pos.data_ptr(),
+            batch, hkv, d, num_pages, page_size, bt.shape[1], _lib.i64_array(k_new.stride()),
+            _lib.i64_array(v_new.stride()), _lib.i64_array(k_cache.stride()), _lib.i64_array(v_cache.stride()),
+            bt.stride(0), stream, st.flags.data_ptr()))
+        if _CHECK_VALUES:
+            _raise_for_flags(int(st.flags.item()))
