@@ -58,7 +58,8 @@ struct __align__(64) DecodeParams {
   const int32_t* csr_last;
   int64_t out_sb, out_sh;
   int batch, hkv, gqa, page_size, num_pages, max_pages;
-  int box_rows;      // R: tokens per TMA box (divides page_size and TT)
+  int box_rows;      // R: tokens per TMA box (a power of two dividing page_size and TT)
+  int box_rows_log2; // log2(R)
   int meta_by_pair;  // merge descriptors indexed by pair (else by partition)
   float scale_log2;  // scale * log2(e)
 };
@@ -110,18 +111,32 @@ struct Traits {
     if constexpr (SWZ) return (uint32_t)(HG * R * SEGW);
     else return (uint32_t)(HG * R * ROW_BYTES < 128 ? 128 : HG * R * ROW_BYTES);
   }
-  // Shared address of 16-byte chunk `c` (0 .. D/8-1) of token `t` (0 .. TT-1),
-  // local head `hl` of a K/V tile at `base`. A box j holds tokens
-  // [j*R, j*R + R) of all HG heads, head-major ([hl][r]).
-  __device__ static __forceinline__ uint32_t kv_addr(uint32_t base, uint32_t t, uint32_t hl, uint32_t c, int R) {
-    const uint32_t j = t / R, r = t % R;
+  // Where token `t` (0 .. TT-1) of local head `hl` lives in a K/V tile: a
+  // box j holds tokens [j*R, j*R + R) of all HG heads, head-major ([hl][r]).
+  // Returns the row's byte offset and its swizzle XOR; lr = log2(R).
+  __device__ static __forceinline__ void kv_row(uint32_t t, uint32_t hl, int lr, uint32_t& rowoff, uint32_t& sw) {
+    const uint32_t R = 1u << lr, j = t >> lr, r = t & (R - 1u);
     if constexpr (SWZ) {
       const uint32_t idx = (j * HG + hl) * R + r;
-      const uint32_t seg = c / CPS, cs = c % CPS;
-      return base + seg * (uint32_t)(kTileRows * SEGW) + idx * SEGW + ((cs ^ swz(idx)) << 4);
+      rowoff = idx * SEGW;
+      sw = swz(idx);
     } else {
-      return base + j * box_pitch(R) + (hl * R + r) * ROW_BYTES + (c << 4);
+      rowoff = j * box_pitch((int)R) + (hl * R + r) * ROW_BYTES;
+      sw = 0u;
     }
+  }
+  // Shared address of 16-byte chunk `c` (0 .. D/8-1) of a row found by kv_row.
+  __device__ static __forceinline__ uint32_t kv_at(uint32_t base, uint32_t rowoff, uint32_t sw, uint32_t c) {
+    if constexpr (SWZ) {
+      return base + (c / CPS) * (uint32_t)(kTileRows * SEGW) + rowoff + (((c % CPS) ^ sw) << 4);
+    } else {
+      return base + rowoff + (c << 4);
+    }
+  }
+  __device__ static __forceinline__ uint32_t kv_addr(uint32_t base, uint32_t t, uint32_t hl, uint32_t c, int lr) {
+    uint32_t rowoff, sw;
+    kv_row(t, hl, lr, rowoff, sw);
+    return kv_at(base, rowoff, sw, c);
   }
   // Query tile: HG*G rows packed (head hl at rows hl*G ..), segment-major.
   __device__ static __forceinline__ uint32_t q_addr(uint32_t base, uint32_t row, uint32_t c) {
@@ -149,12 +164,22 @@ struct Cursor {
 __device__ __forceinline__ int clamp_seq(int raw, int cap) { return raw < 0 ? 0 : (raw > cap ? cap : raw); }
 
 // Partition w of W covers global tiles [begin(w), begin(w+1)).
+// floor(a / b) for 0 <= a < 2^52 and 0 < b < 2^31: a double-precision
+// quotient corrected to the exact integer result (a 64-bit integer division
+// would inline a long instruction sequence at every use).
+__device__ __forceinline__ int64_t div_floor(int64_t a, int64_t b) {
+  int64_t q = (int64_t)((double)a / (double)b);
+  if (q * b > a) --q;
+  else if ((q + 1) * b <= a) ++q;
+  return q;
+}
+
 __device__ __forceinline__ int part_begin(int64_t w, int64_t total, int64_t parts) {
-  return (int)((w * total) / parts);
+  return (int)div_floor(w * total, parts);
 }
 // The partition owning global tile t: the largest w with begin(w) <= t.
 __device__ __forceinline__ int part_owner(int64_t t, int64_t total, int64_t parts) {
-  return (int)(((t + 1) * parts - 1) / total);
+  return (int)div_floor((t + 1) * parts - 1, total);
 }
 
 }  // namespace pad

@@ -157,17 +157,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
   // loads their page ids now, overlapping the seq_lens round trip below.
   const int ncap = tiles_of<TR>(cap);
   // (no guess for a CSR index: its rows have no fixed width)
-  const int64_t tg_total = p.csr_indptr == nullptr ? (int64_t)p.batch * ngroups * ncap : 0;
+  const int tg_total = p.csr_indptr == nullptr ? p.batch * ngroups * ncap : 0;  // < 2^30 (host-checked)
   const int tg0 = tg_total > 0 ? part_begin(w, tg_total, W) : 0;
   int gpid[S][TR::NB_PER_LANE];
   if (warp == kConsumerWarps) {
 #pragma unroll
     for (int k = 0; k < S; ++k) {
-      const int64_t t = (int64_t)tg0 + k;
+      const int t = tg0 + k;
       if (t < tg_total) {
         const int per_seq = ngroups * ncap;
-        const int r = (int)(t % per_seq);
-        const Cursor gc{(int)(t / per_seq), r / ncap, r % ncap, ncap, cap, 0, (t / per_seq) * p.bt_stride};
+        const int bq = t / per_seq, r = t - bq * per_seq;
+        const Cursor gc{bq, r / ncap, r % ncap, ncap, cap, 0, (int64_t)bq * p.bt_stride};
         load_page_ids<TR>(p, gc, lane, gpid[k]);
       }
     }
@@ -234,6 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     if (seq_of(p, sseq, b, cap) == 0) {
       if (p.meta_by_pair && tid < ngroups) p.ws_meta[b * ngroups + tid] = make_int4(-1, 0, 0, 0);
       const int hq = p.hkv * G;
+#pragma unroll 1
       for (int x = tid; x < hq * (D / 2); x += kThreads) {
         const int hh = x / (D / 2), d = (x % (D / 2)) * 2;
         *reinterpret_cast<__half2*>(p.out + b * p.out_sb + hh * p.out_sh + d) = __floats2half2_rn(0.f, 0.f);
@@ -268,9 +269,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     for (int k = 0; k < S; ++k) {
       if (k < ntiles) {
         // reuse the speculative ids when the real tile is the guessed one
-        const int64_t t = (int64_t)tg0 + k;
-        const bool hit = t < tg_total && la.b == (int)(t / per_seq) && la.hg == (int)(t % per_seq) / ncap &&
-                         la.i == (int)(t % per_seq) % ncap;
+        const int t = tg0 + k;
+        const int bq = t < tg_total ? t / per_seq : -1, r = t - bq * per_seq;
+        const bool hit = bq >= 0 && la.b == bq && la.hg == r / ncap && la.i == r % ncap;
         if (hit) {
 #pragma unroll
           for (int u = 0; u < TR::NB_PER_LANE; ++u) pid[k][u] = gpid[k][u];
@@ -389,8 +390,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
   if (ntiles <= 0) return;
   const int hl = warp / WPH;               // local KV head this warp serves
   const uint32_t t_base = (warp % WPH) * 16;  // its 16 tokens within the tile
-  const int R = p.box_rows;
-  const int gl = 2 * (lane & 3);            // first query row (within an n8 tile) this lane owns
+  const int lr = p.box_rows_log2;
+  const int gl = 2 * (lane & 3);
+  // this lane's ldmatrix rows: K (A operand of S^T) and V (A operand of O^T)
+  uint32_t k_row, k_sw, v_row, v_sw;
+  TR::kv_row(t_base + (lane & 7) + ((lane >> 3) & 1) * 8, hl, lr, k_row, k_sw);
+  TR::kv_row(t_base + (lane & 7) + ((lane >> 4) & 1) * 8, hl, lr, v_row, v_sw);            // first query row (within an n8 tile) this lane owns
   uint32_t qf[KSTEPS][NT][2];
   float acc[KSTEPS][NT][4];
   float m_run[NT][2], l_run[NT][2];
@@ -460,7 +465,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
         // tokens contribute exactly 0; K rows are masked through the scores.
         for (int x = lane; x < (16 - nv) * (D / 8); x += 32) {
           const uint32_t t = t_base + nv + x / (D / 8), cc = x % (D / 8);
-          asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(TR::kv_addr(vb, t, hl, cc, R)), "r"(0)
+          asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(TR::kv_addr(vb, t, hl, cc, lr)), "r"(0)
                        : "memory");
         }
         fence_proxy_async_smem();
@@ -473,8 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
 #pragma unroll
       for (int kk = 0; kk < KSTEPS; ++kk) {
         uint32_t a0, a1, a2, a3;
-        ldsm_x4(TR::kv_addr(kb, t_base + (lane & 7) + ((lane >> 3) & 1) * 8, hl, kk * 2 + (lane >> 4), R), a0, a1,
-                a2, a3);
+        ldsm_x4(TR::kv_at(kb, k_row, k_sw, kk * 2 + (lane >> 4)), a0, a1, a2, a3);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) mma_16816(sc[nt], a0, a1, a2, a3, qf[kk][nt][0], qf[kk][nt][1]);
       }
@@ -522,8 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
 #pragma unroll
       for (int mt = 0; mt < KSTEPS; ++mt) {
         uint32_t a0, a1, a2, a3;
-        ldsm_x4_trans(TR::kv_addr(vb, t_base + (lane & 7) + ((lane >> 4) & 1) * 8, hl, mt * 2 + ((lane >> 3) & 1), R),
-                      a0, a1, a2, a3);
+        ldsm_x4_trans(TR::kv_at(vb, v_row, v_sw, mt * 2 + ((lane >> 3) & 1)), a0, a1, a2, a3);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) mma_16816(acc[mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
       }
@@ -599,7 +602,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
         // the WPH warps of a head add their rescaled O^T into one buffer in a
         // fixed order (deterministic results): warp 0 stores, the others add
         float* buf = epi + hl * (8 * NT * D);
-#pragma unroll
+#pragma unroll 1
         for (int step = 0; step < WPH; ++step) {
           if ((int)(t_base / 16) == step) {
 #pragma unroll
@@ -619,6 +622,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
         const int ctid = warp * 32 + lane;
         if (!split) {
           __half* obase = p.out + dsc.b * p.out_sb + (int64_t)(dsc.hg * HG * G) * p.out_sh;
+#pragma unroll 1
           for (int x = ctid; x < HG * G * (D / 2); x += 32 * kConsumerWarps) {
             const int row = x / (D / 2), d = (x % (D / 2)) * 2;
             const int h = row / G, g = row % G;
@@ -629,6 +633,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
           }
         } else {
           float4* o4 = reinterpret_cast<float4*>(p.ws_o + (int64_t)dsc.slot * HG * G * D);
+#pragma unroll 1
           for (int x = ctid; x < HG * G * (D / 4); x += 32 * kConsumerWarps) {
             const int row = x / (D / 4), d = (x % (D / 4)) * 4;
             const int h = row / G, g = row % G;

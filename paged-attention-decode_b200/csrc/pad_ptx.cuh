@@ -85,16 +85,22 @@ __device__ __forceinline__ bool mbar_spin_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
-// Bounded wait for the phase of `bar` with the given parity. Returns false if
-// `timeout_ns` of wall time passed first (the caller records the failure and
-// unwinds); never spins forever.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
+// Slow path of mbar_wait_bounded, kept out of line: one shared copy of the
+// polling loop instead of one per call site (the kernels stay small).
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63u) == 0 && globaltimer_ns() - t0 > timeout_ns) return false;
   }
+}
+
+// Bounded wait for the phase of `bar` with the given parity. Returns false if
+// `timeout_ns` of wall time passed first (the caller records the failure and
+// unwinds); never spins forever.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, timeout_ns);
 }
 
 // A read-only global load the compiler may not move (issued where written,
