@@ -409,7 +409,21 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, const i
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   void* args[] = {&prm};
-  e = cudaLaunchKernel(in.kernel, dim3((unsigned)plan.partitions), dim3(kThreads), args, (size_t)in.smem_bytes, s);
+  {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)plan.partitions);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = (size_t)in.smem_bytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    // overlap this launch with the tail of whatever precedes it in the stream
+    // (the kernel waits on griddepcontrol before touching global memory)
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelExC(&cfg, in.kernel, args);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "launching the decode kernel");
   if (plan.partitions > 1) {
     const float* a0 = prm.ws_o;

@@ -88,7 +88,9 @@ struct Traits {
   static constexpr int NB_MAX = SWZ ? TT / 8 : TT;  // TMA boxes per tile
   static constexpr int NB_PER_LANE = (NB_MAX + 31) / 32;
   // Cross-warp merge buffer (only when several warps share a head).
-  static constexpr int EPI_BYTES = WPH > 1 ? HG * 8 * NT * D * 4 : 0;
+  // Two buffers (a two-level add tree) when 4 or more warps share a head.
+  static constexpr int EPI_BUFS = WPH >= 4 ? 2 : 1;
+  static constexpr int EPI_BYTES = WPH > 1 ? EPI_BUFS * HG * 8 * NT * D * 4 : 0;
   static constexpr int MISC_BYTES = 4096 + kSeqCache * 4;  // + cached seq_lens
   // Query tiles in flight: two (one segment ahead) unless that costs a stage.
   static constexpr int QSLOTS = (kSmemBudget - (1024 + 2 * Q_BYTES + EPI_BYTES + MISC_BYTES)) / STAGE_BYTES >= 3 ? 2 : 1;

@@ -152,6 +152,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     fence_mbar_init();
   }
 
+  // Launched as a programmatic dependent of the previous kernel in the
+  // stream: everything above touches only this CTA's shared memory; wait for
+  // the previous kernel's results (and for it to finish with the workspace)
+  // before reading any input or writing any global memory.
+  pdl_wait_primary();
+
   // ---- speculative page ids: the producer guesses its first tiles assuming
   // every sequence fills its block-table row (true for uniform batches) and
   // loads their page ids now, overlapping the seq_lens round trip below.
@@ -599,12 +605,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
             scl[nt][j] = ex2(m_run[nt][j] - Mu);
             if (t_base == 0 && (lane >> 2) == 0) sML[hl * 8 * NT + g] = make_float2(Mu, L);
           }
-        // the WPH warps of a head add their rescaled O^T into one buffer in a
-        // fixed order (deterministic results): warp 0 stores, the others add
-        float* buf = epi + hl * (8 * NT * D);
+        // the WPH warps of a head add their rescaled O^T into EPI_BUFS buffers
+        // in a fixed order (deterministic results): warp tb stores (first
+        // step) or adds into buffer tb % EPI_BUFS at step tb / EPI_BUFS
+        constexpr int NB = TR::EPI_BUFS, BUF = HG * 8 * NT * D;
+        const int tb = (int)(t_base / 16);
+        float* buf = epi + (tb % NB) * BUF + hl * (8 * NT * D);
 #pragma unroll 1
-        for (int step = 0; step < WPH; ++step) {
-          if ((int)(t_base / 16) == step) {
+        for (int step = 0; step < WPH / NB; ++step) {
+          if (tb / NB == step) {
 #pragma unroll
             for (int mt = 0; mt < KSTEPS; ++mt)
 #pragma unroll
@@ -629,7 +638,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
             const float L = sML[h * 8 * NT + g].y;
             const float inv = L > 0.f ? 1.f / L : 0.f;
             const float* src = epi + h * (8 * NT * D) + g * D + d;
-            *reinterpret_cast<__half2*>(obase + row * p.out_sh + d) = __floats2half2_rn(src[0] * inv, src[1] * inv);
+            float v0 = src[0], v1 = src[1];
+            if constexpr (NB == 2) {
+              v0 += src[BUF];
+              v1 += src[BUF + 1];
+            }
+            *reinterpret_cast<__half2*>(obase + row * p.out_sh + d) = __floats2half2_rn(v0 * inv, v1 * inv);
           }
         } else {
           float4* o4 = reinterpret_cast<float4*>(p.ws_o + (int64_t)dsc.slot * HG * G * D);
@@ -637,7 +651,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
           for (int x = ctid; x < HG * G * (D / 4); x += 32 * kConsumerWarps) {
             const int row = x / (D / 4), d = (x % (D / 4)) * 4;
             const int h = row / G, g = row % G;
-            o4[x] = *reinterpret_cast<const float4*>(epi + h * (8 * NT * D) + g * D + d);
+            float4 v = *reinterpret_cast<const float4*>(epi + h * (8 * NT * D) + g * D + d);
+            if constexpr (NB == 2) {
+              const float4 u = *reinterpret_cast<const float4*>(epi + BUF + h * (8 * NT * D) + g * D + d);
+              v = make_float4(v.x + u.x, v.y + u.y, v.z + u.z, v.w + u.w);
+            }
+            o4[x] = v;
           }
           for (int x = ctid; x < HG * G; x += 32 * kConsumerWarps)
             p.ws_ml[(int64_t)dsc.slot * HG * G + x] = sML[(x / G) * 8 * NT + x % G];
@@ -671,6 +690,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const float* __res
   constexpr int PG = kMergeThreads / C4;   // partial groups folded in parallel
   __shared__ float red_o[PG][DC];
   __shared__ float red_m[PG], red_l[PG];
+  pdl_launch_dependents();  // the next decode may start its own set-up
   pdl_wait_primary();
   const int w = blockIdx.x, y = blockIdx.y, tid = threadIdx.x;
   if (tid == 0) PAD_STAMP_MIN(0);
