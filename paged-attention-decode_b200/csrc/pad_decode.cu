@@ -41,7 +41,8 @@ int cuda_fail(cudaError_t e, const char* what) {
 struct Instance {
   const void* kernel;          // decode_stream_kernel<TR>
   const void* merge_small;     // merge_kernel<D, 128>: few partials per split pair
-  const void* merge_large;     // merge_kernel<D, 256, D/32>: many partials (long context), D split over CTAs
+  const void* merge_mid;       // merge_kernel<D, 256, D/32, 4>: a handful of partials, D split over CTAs
+  const void* merge_large;     // merge_kernel<D, 256, D/32, 8>: many partials (long context)
   int merge_dsplit;
   int smem_bytes;
   int segw;                    // bytes per row segment (TMA box inner extent)
@@ -55,8 +56,9 @@ Instance make_instance() {
   using TR = Traits<D, NT, HG, SWZ>;
   Instance in;
   in.kernel = reinterpret_cast<const void*>(&decode_stream_kernel<TR>);
-  in.merge_small = reinterpret_cast<const void*>(&merge_kernel<D, 128, 1>);
-  in.merge_large = reinterpret_cast<const void*>(&merge_kernel<D, 256, (D >= 64 ? D / 32 : 1)>);
+  in.merge_small = reinterpret_cast<const void*>(&merge_kernel<D, 128, 1, 4>);
+  in.merge_mid = reinterpret_cast<const void*>(&merge_kernel<D, 256, (D >= 64 ? D / 32 : 1), 4>);
+  in.merge_large = reinterpret_cast<const void*>(&merge_kernel<D, 256, (D >= 64 ? D / 32 : 1), 8>);
   in.merge_dsplit = D >= 64 ? D / 32 : 1;
   in.smem_bytes = TR::SMEM_BYTES;
   in.segw = TR::SEGW;
@@ -446,7 +448,8 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, const i
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelExC(&cfg, wide ? in.merge_large : in.merge_small, margs);
+    const bool deep = plan.partitions > 16 * batch * ngroups;  // > 16 partials per pair: 8 loads in flight
+    e = cudaLaunchKernelExC(&cfg, wide ? (deep ? in.merge_large : in.merge_mid) : in.merge_small, margs);
     if (e != cudaSuccess) return cuda_fail(e, "launching the merge kernel");
   }
   return PAD_OK;

@@ -676,10 +676,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
 // (analysis/split_k_derivation.md:44-65; a partial with m_s = -inf weighs 0
 // and its O is not read, the guard of analysis/split_k_derivation.md:67-86).
 // Each thread folds a strided subset of the partials with an online LSE
-// (loads issued four at a time), then the per-thread states are combined
+// (loads issued 4 or 8 at a time), then the per-thread states are combined
 // through shared memory. Launched as a programmatic dependent of the decode
 // kernel: it waits on griddepcontrol before reading the partials.
-template <int D, int kMergeThreads, int DS>
+template <int D, int kMergeThreads, int DS, int UNR>
 __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const float* __restrict__ ws_o,
                                                               const float2* __restrict__ ws_ml,
                                                               const int4* __restrict__ ws_meta,
@@ -700,11 +700,11 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const float* __res
   const int c = tid % C4 + blockIdx.z * C4, sg = tid / C4;
   float m = -INFINITY, l = 0.f;
   float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int s = sg; s < ns; s += 4 * PG) {
-    float2 ml[4];
-    float4 o[4];
+  for (int s = sg; s < ns; s += UNR * PG) {
+    float2 ml[UNR];
+    float4 o[UNR];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < UNR; ++u) {
       const int su = s + u * PG;
       ml[u] = make_float2(-INFINITY, 0.f);
       if (su < ns) {
@@ -714,7 +714,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const float* __res
       }
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < UNR; ++u) {
       if (ml[u].x == -INFINITY) continue;
       const float mn = fmaxf(m, ml[u].x);
       const float al = ex2(m - mn), be = ex2(ml[u].x - mn);
