@@ -37,7 +37,12 @@ def _worker(rank, world, port, q):
         _, full = decode_sharded(qh, kh, vh, torch.from_numpy(c.block_table), torch.from_numpy(c.seq_lens),
                                  world=world, rank=rank, device=torch.device("cuda", rank), shuffle_seed=rank)
         if rank == 0:
-            q.put(full.float().cpu().numpy())
+            # send back only scalars: a large object in the queue would block
+            # this child's exit while the parent waits in join()
+            ref = oracle.decode_c(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens)
+            got = full.float().cpu().numpy()
+            err = np.abs(got - ref)
+            q.put((bool(np.all(err <= 2e-3 + 1e-2 * np.abs(ref))), float(err.max())))
     finally:
         dist.destroy_process_group()
 
@@ -50,6 +55,7 @@ def _port():
     return p
 
 
+@pytest.mark.timeout(240)
 def test_sharded_decode_matches_oracle():
     if not torch.cuda.is_available():
         pytest.skip("needs a CUDA device")
@@ -69,4 +75,5 @@ def test_sharded_decode_matches_oracle():
     ctx = mp.get_context("spawn")
     qq = ctx.Queue()
     mp.start_processes(_worker, args=(world, _port(), qq), nprocs=world, join=True, start_method="spawn")
-    assert_parity(qq.get(timeout=120), ref, f"world={world}")
+    ok, max_err = qq.get(timeout=60)
+    assert ok and max_err <= 2e-3, f"world={world}: max abs err {max_err:.3e}"
