@@ -551,6 +551,12 @@ int pad_debug_trace_read(uint64_t* host, size_t n) {
   cudaError_t e = cudaMemcpyFromSymbol(host, g_pad_trace, n * sizeof(uint64_t));
   return e == cudaSuccess ? PAD_OK : cuda_fail(e, "trace read");
 }
+int pad_debug_trace_reset(void) {
+  void* a = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&a, g_pad_trace);
+  if (e == cudaSuccess) e = cudaMemset(a, 0, sizeof(g_pad_trace));
+  return e == cudaSuccess ? PAD_OK : cuda_fail(e, "trace reset");
+}
 #endif
 
 }  // extern "C"

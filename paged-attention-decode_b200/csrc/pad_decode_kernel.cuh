@@ -38,6 +38,7 @@ constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s: no legitimate wait c
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kSmemBudget = 227 * 1024;
 constexpr int kSeqCache = 1024;   // seq_lens kept in shared memory when batch <= this
+constexpr int kFastBatch = 256;   // largest batch the producer's fast start checks (8 loads per lane)
 
 struct __align__(64) DecodeParams {
   CUtensorMap tm_k;  // dims {D, page_size, Hkv, num_pages}, box {SEG, R, HG, 1}

@@ -2,6 +2,8 @@
 // for the design summary and the shared definitions).
 #pragma once
 
+#include <climits>
+
 #include "pad_b200.h"
 #include "pad_decode_kernel.cuh"
 
@@ -13,14 +15,15 @@ __device__ __forceinline__ void raise_flag(const DecodeParams& p, int bits) {
 
 #ifdef PAD_TRACE
 // Development-only timeline: per-CTA %globaltimer stamps (compile with -DPAD_TRACE).
-__device__ uint64_t g_pad_trace[4096 * 8];
-#define PAD_STAMP(i) (g_pad_trace[blockIdx.x * 8 + (i)] = globaltimer_ns())
-#define PAD_STAMP_MIN(i) atomicMin((unsigned long long*)&g_pad_trace[4096 * 8 - 2 + (i)], (unsigned long long)globaltimer_ns())
-#define PAD_STAMP_MAX(i) atomicMax((unsigned long long*)&g_pad_trace[4096 * 8 - 2 + (i)], (unsigned long long)globaltimer_ns())
+// Decode CTAs own 32 slots each; merge CTAs own 4 slots each after them.
+__device__ uint64_t g_pad_trace[1024 * 32 + 4096 * 4];
+#define PAD_STAMP(i) (g_pad_trace[blockIdx.x * 32 + (i)] = globaltimer_ns())
+#define PAD_MSTAMP(i)                                                                                  \
+  (g_pad_trace[1024 * 32 + ((blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * 4 + (i)] = \
+       globaltimer_ns())
 #else
 #define PAD_STAMP(i) ((void)0)
-#define PAD_STAMP_MIN(i) ((void)0)
-#define PAD_STAMP_MAX(i) ((void)0)
+#define PAD_MSTAMP(i) ((void)0)
 #endif
 
 template <class TR>
@@ -28,10 +31,6 @@ __device__ __forceinline__ int tiles_of(int seq) {
   return (seq + TR::TT - 1) / TR::TT;
 }
 
-// Step a cursor to the next tile of the flattened (sequence, head group,
-// tile) list; past the end it reports n = 0.
-// seq_lens of sequence b, clamped: from the shared-memory copy made by the
-// prologue when the batch fits in it, else from global memory.
 // seq_len of sequence b as given (dense: seq_lens[b]; CSR: from the page
 // count and the last page's fill).
 __device__ __forceinline__ int raw_seq(const DecodeParams& p, int b) {
@@ -45,12 +44,18 @@ __device__ __forceinline__ int64_t row_base(const DecodeParams& p, int b) {
   return p.csr_indptr == nullptr ? (int64_t)b * p.bt_stride : (int64_t)__ldg(p.csr_indptr + b);
 }
 
+// seq_len of sequence b, clamped: from the shared-memory copy made by the
+// prologue scan when the batch fits in it, else from global memory.
 __device__ __forceinline__ int seq_of(const DecodeParams& p, const int* sseq, int b, int cap) {
   return b < kSeqCache ? sseq[b] : clamp_seq(raw_seq(p, b), cap);
 }
 
+// Step a cursor to the next tile of the flattened (sequence, head group,
+// tile) list; past the end it reports n = 0. useq >= 0: every sequence has
+// seq_len useq (no seq_lens lookup).
 template <class TR>
-__device__ __forceinline__ void cursor_next(Cursor& c, const DecodeParams& p, int cap, int ngroups, const int* sseq) {
+__device__ __forceinline__ void cursor_next(Cursor& c, const DecodeParams& p, int cap, int ngroups, const int* sseq,
+                                            int useq) {
   if (++c.i < c.n) return;
   c.i = 0;
   c.pair_start += c.n;
@@ -61,10 +66,19 @@ __device__ __forceinline__ void cursor_next(Cursor& c, const DecodeParams& p, in
       c.n = 0;
       return;
     }
-    c.seq = seq_of(p, sseq, c.b, cap);
+    c.seq = useq >= 0 ? useq : seq_of(p, sseq, c.b, cap);
     c.n = tiles_of<TR>(c.seq);
     c.base = row_base(p, c.b);
   } while (c.n == 0);
+}
+
+// Cursor at global tile t of a dense batch whose sequences all have seq_len
+// seq > 0 (the tile list is then a plain 3-level index).
+template <class TR>
+__device__ __forceinline__ Cursor uniform_cursor(int t, int seq, int ngroups, int64_t bt_stride) {
+  const int n = tiles_of<TR>(seq), per = ngroups * n;
+  const int b = t / per, r = t - b * per, hg = r / n, i = r - hg * n;
+  return Cursor{b, hg, i, n, seq, t - i, (int64_t)b * bt_stride};
 }
 
 // Page ids of the TMA boxes of the tile at cursor `c`: lane l loads boxes
@@ -118,6 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
   int* scan = reinterpret_cast<int*>(sML + HG * 8 * NT);             // [kThreads/32]
   volatile int* abort_flag = scan + 12;
   int* cur_smem = scan + 16;                                         // Cursor as 6 ints
+  int* range_smem = scan + 40;                                       // t0, t1, total
   int* sink = scan + 24;                                             // [consumer warps] scratch
   int* sseq = scan + 64;                                             // [kSeqCache] clamped seq_lens
 
@@ -134,7 +149,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     prefetch_tmap(&p.tm_q);
   }
 
-  // ---- set-up: zero the query tiles (rows past HG*G stay zero), init barriers
+  // ---- set-up, on this CTA's shared memory only (so before the wait on the
+  // previous kernel): zero the query tiles (rows past HG*G stay zero), init
+  // the barriers, make both visible to the async proxy and to every warp.
   for (int x = tid; x < TR::QSLOTS * TR::Q_BYTES / 16; x += kThreads)
     reinterpret_cast<uint4*>(qtiles)[x] = make_uint4(0, 0, 0, 0);
   if (tid == 0) {
@@ -151,140 +168,104 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     cur_smem[0] = -1;
     fence_mbar_init();
   }
+  fence_proxy_async_smem();  // zeroed query tiles before any TMA write to them
+  __syncthreads();
+
+  // A dense batch of at most kFastBatch sequences whose rows are all full
+  // (seq_len == cap) has a tile list known from the parameters alone, so the
+  // producer can fetch its first page ids in the same round trip as seq_lens.
+  const int ncap = tiles_of<TR>(cap);
+  const int tg_total = (p.csr_indptr == nullptr && p.batch <= kFastBatch) ? p.batch * ngroups * ncap : 0;
+  const int tg0 = tg_total > 0 ? part_begin(w, tg_total, W) : 0;
+  const int tg1 = tg_total > 0 ? part_begin(w + 1, tg_total, W) : 0;
 
   // Launched as a programmatic dependent of the previous kernel in the
   // stream: everything above touches only this CTA's shared memory; wait for
   // the previous kernel's results (and for it to finish with the workspace)
   // before reading any input or writing any global memory.
   pdl_wait_primary();
-
-  // ---- speculative page ids: the producer guesses its first tiles assuming
-  // every sequence fills its block-table row (true for uniform batches) and
-  // loads their page ids now, overlapping the seq_lens round trip below.
-  const int ncap = tiles_of<TR>(cap);
-  // (no guess for a CSR index: its rows have no fixed width)
-  const int tg_total = p.csr_indptr == nullptr ? p.batch * ngroups * ncap : 0;  // < 2^30 (host-checked)
-  const int tg0 = tg_total > 0 ? part_begin(w, tg_total, W) : 0;
-  int gpid[S][TR::NB_PER_LANE];
-  if (warp == kConsumerWarps) {
-#pragma unroll
-    for (int k = 0; k < S; ++k) {
-      const int t = tg0 + k;
-      if (t < tg_total) {
-        const int per_seq = ngroups * ncap;
-        const int bq = t / per_seq, r = t - bq * per_seq;
-        const Cursor gc{bq, r / ncap, r % ncap, ncap, cap, 0, (int64_t)bq * p.bt_stride};
-        load_page_ids<TR>(p, gc, lane, gpid[k]);
-      }
-    }
-  }
-
-  // ---- block-wide exclusive scan of tiles per sequence (x head groups)
-  const int per = (p.batch + kThreads - 1) / kThreads;
-  const int b_lo = min(p.batch, tid * per), b_hi = min(p.batch, b_lo + per);
-  int local = 0, bad = 0, any_empty = 0;
-  for (int b = b_lo; b < b_hi; ++b) {
-    const int raw = raw_seq(p, b);
-    bad |= (raw < 0 || raw > cap);
-    const int sq = clamp_seq(raw, cap);
-    if (b < kSeqCache) sseq[b] = sq;
-    any_empty |= (sq == 0);
-    local += tiles_of<TR>(sq);
-  }
-  local *= ngroups;
-  int incl = local;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += y;
-  }
-  if (lane == 31) scan[warp] = incl;
-  any_empty = __syncthreads_or(any_empty);
-  int excl = incl - local, total = 0;
-  for (int x = 0; x < kThreads / 32; ++x) {
-    const int v = scan[x];
-    if (x < warp) excl += v;
-    total += v;
-  }
-  if (bad && w == 0) raise_flag(p, PAD_FLAG_SEQ_LEN_RANGE);
-  const int t0 = total > 0 ? part_begin(w, total, W) : 0;
-  const int t1 = total > 0 ? part_begin(w + 1, total, W) : 0;
-  if (t0 < total && excl <= t0 && t0 < excl + local) {
-    int acc_t = excl;
-    for (int b = b_lo; b < b_hi; ++b) {
-      const int seq = seq_of(p, sseq, b, cap);
-      const int n = tiles_of<TR>(seq);
-      const int tb = n * ngroups;
-      if (t0 < acc_t + tb) {
-        const int o = t0 - acc_t;
-        cur_smem[0] = b;
-        cur_smem[1] = o / n;
-        cur_smem[2] = o % n;
-        cur_smem[3] = n;
-        cur_smem[4] = seq;
-        cur_smem[5] = acc_t + (o / n) * n;
-        break;
-      }
-      acc_t += tb;
-    }
-  }
-  fence_proxy_async_smem();  // zeroed query tiles before any TMA write to them
-  __syncthreads();
-  if (tid == 0) PAD_STAMP(1);
-  // the merge kernel may be scheduled now; it waits for this grid's results
-  if (tid == 0) pdl_launch_dependents();
-
-  // ---- zero output rows of empty sequences (src/reference.py:32-34)
-  // (only when the scan saw one: no extra global reads on the common path)
-  for (int b = w; any_empty && b < p.batch; b += (int)W) {
-    if (seq_of(p, sseq, b, cap) == 0) {
-      if (p.meta_by_pair && tid < ngroups) p.ws_meta[b * ngroups + tid] = make_int4(-1, 0, 0, 0);
-      const int hq = p.hkv * G;
-#pragma unroll 1
-      for (int x = tid; x < hq * (D / 2); x += kThreads) {
-        const int hh = x / (D / 2), d = (x % (D / 2)) * 2;
-        *reinterpret_cast<__half2*>(p.out + b * p.out_sb + hh * p.out_sh + d) = __floats2half2_rn(0.f, 0.f);
-      }
-    }
-  }
-
-  const int ntiles = t1 - t0;
+  if (tid == 0) PAD_STAMP(10);
 
   if (warp == kConsumerWarps) {
     // =============================== producer warp ===============================
+    // Fast start: when every seq_len is the same value L the partition's
+    // range and first cursor have a closed form, so the producer needs no
+    // block-wide scan. L == cap also validates the page ids loaded on the
+    // guess above; otherwise they are loaded once L is known. Any other batch
+    // takes the range and cursor from the consumer warps' scan.
+    int t0 = 0, t1 = 0, total = 0, useq = -1;
+    bool have_ids = false;
+    Cursor c{-1, 0, 0, 0, 0, 0, 0};
+    int pid[S][TR::NB_PER_LANE];
+    if (tg_total > 0) {
+      {
+        Cursor g = uniform_cursor<TR>(tg0, cap, ngroups, p.bt_stride);
+#pragma unroll
+        for (int k = 0; k < S; ++k) {
+          if (tg0 + k < tg1) {
+            load_page_ids<TR>(p, g, lane, pid[k]);
+            cursor_next<TR>(g, p, cap, ngroups, sseq, cap);
+          }
+        }
+      }
+      int mn = INT_MAX, mx = INT_MIN;
+#pragma unroll
+      for (int u = 0; u < kFastBatch / 32; ++u) {
+        const int b = lane + 32 * u;
+        if (b < p.batch) {
+          const int v = ld_nc_early(p.seq_lens + b);
+          mn = min(mn, v);
+          mx = max(mx, v);
+        }
+      }
+      mn = __reduce_min_sync(0xffffffffu, mn);
+      mx = __reduce_max_sync(0xffffffffu, mx);
+      if (mn == mx && mn > 0 && mn <= cap) {
+        useq = mn;
+        if (mn == cap) {
+          t0 = tg0;
+          t1 = tg1;
+          total = tg_total;
+          have_ids = true;
+        } else {
+          total = p.batch * ngroups * tiles_of<TR>(mn);
+          t0 = part_begin(w, total, W);
+          t1 = part_begin(w + 1, total, W);
+        }
+        if (t0 < total) c = uniform_cursor<TR>(t0, useq, ngroups, p.bt_stride);
+      }
+    }
+    if (useq >= 0) {
+      named_barrier_arrive(3, kThreads);  // the consumers' hand-off is not needed
+    } else {
+      named_barrier(3, kThreads);
+      t0 = range_smem[0];
+      t1 = range_smem[1];
+      total = range_smem[2];
+      c = Cursor{cur_smem[0], cur_smem[1], cur_smem[2], cur_smem[3], cur_smem[4], cur_smem[5], 0};
+      if (c.b >= 0) c.base = row_base(p, c.b);
+    }
+    const int ntiles = t1 - t0;
     if (lane == 0 && !p.meta_by_pair) p.ws_meta[w] = make_int4(-1, 0, 0, 0);
     if (lane == 0) PAD_STAMP(7);
     if (ntiles <= 0) {
       // An empty partition (more partitions than tiles) can sit between the
       // first and last partition of a split pair; it owns a partial slot of
       // that pair, which it marks empty (m = -inf, l = 0) for every head.
-      if (cur_smem[0] >= 0 && cur_smem[5] < t0) {
-        const int slot = cur_smem[0] * ngroups + cur_smem[1] + w;
+      if (c.b >= 0 && c.pair_start < t0) {
+        const int slot = c.b * ngroups + c.hg + w;
         for (int x = lane; x < HG * G; x += 32) p.ws_ml[(int64_t)slot * HG * G + x] = make_float2(-INFINITY, 0.f);
       }
       return;
     }
     const int R = p.box_rows;
     const uint64_t kv_policy = l2_evict_first_policy();
-    Cursor c{cur_smem[0], cur_smem[1], cur_smem[2], cur_smem[3], cur_smem[4], cur_smem[5], 0};
-    c.base = row_base(p, c.b);
     Cursor la = c;
-    int pid[S][TR::NB_PER_LANE];
-    const int per_seq = ngroups * ncap;
 #pragma unroll
     for (int k = 0; k < S; ++k) {
       if (k < ntiles) {
-        // reuse the speculative ids when the real tile is the guessed one
-        const int t = tg0 + k;
-        const int bq = t < tg_total ? t / per_seq : -1, r = t - bq * per_seq;
-        const bool hit = bq >= 0 && la.b == bq && la.hg == r / ncap && la.i == r % ncap;
-        if (hit) {
-#pragma unroll
-          for (int u = 0; u < TR::NB_PER_LANE; ++u) pid[k][u] = gpid[k][u];
-        } else {
-          load_page_ids<TR>(p, la, lane, pid[k]);
-        }
-        cursor_next<TR>(la, p, cap, ngroups, sseq);
+        if (!have_ids) load_page_ids<TR>(p, la, lane, pid[k]);
+        cursor_next<TR>(la, p, cap, ngroups, sseq, useq);
       }
     }
     if (lane == 0) PAD_STAMP(5);
@@ -317,42 +298,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
       const int pair = c.b * ngroups + c.hg;
       const bool split = !(c.pair_start >= t0 && c.pair_start + c.n <= t1);
       const int qs = segs % TR::QSLOTS;
-      if (first) {
-        // the query tile of this segment: wait until its ring slot is free
-        if (segs >= TR::QSLOTS) ok = mbar_wait_bounded(&qempty[qs], ((segs / TR::QSLOTS) - 1) & 1, kWaitTimeoutNs);
+      // the query tile of a new segment: wait until its ring slot is free
+      if (first && segs >= TR::QSLOTS) {
+        ok = mbar_wait_bounded(&qempty[qs], ((segs / TR::QSLOTS) - 1) & 1, kWaitTimeoutNs);
         if (!__all_sync(0xffffffffu, ok)) break;
-        if (lane == 0) {
-          if (k == 0) PAD_STAMP(6);
-          mbar_arrive_expect_tx(&qfull[qs], qbytes);
-#pragma unroll
-          for (int sg = 0; sg < TR::NSEG; ++sg)
-            tma_load_3d(qtiles + qs * TR::Q_BYTES + sg * TR::QROWS * TR::SEGW, &p.tm_q, &qfull[qs],
-                        sg * (TR::SEGW / 2), c.hg * HG * G, c.b);
-        }
       }
-      if (lane == 0) {
-        TileDesc dsc;
-        dsc.b = c.b;
-        dsc.hg = c.hg;
-        dsc.i = c.i;
-        dsc.seq = c.seq;
-        dsc.flags = (first ? kFirst : 0) | (last ? kLast : 0) | (split ? kSplit : 0);
-        // Partial slots: pair p uses slots [p + owner(start_p), ...], one per
-        // partition touching it; partition w writes slot p + w. These ranges
-        // are disjoint across pairs and stay below partitions + pairs.
-        dsc.slot = pair + w;
-        dsc.qslot = qs;
-        dsc.pad = 0;
-        descs[s] = dsc;
-        // The partition holding a pair's first tile publishes its merge
-        // descriptor (indexed by pair or by partition, see meta_by_pair).
-        if (c.i == 0 && (split || p.meta_by_pair)) {
-          const int last_owner = part_owner((int64_t)c.pair_start + c.n - 1, total, W);
-          p.ws_meta[p.meta_by_pair ? pair : w] =
-              split ? make_int4(pair, pair + w, last_owner - w + 1, 1) : make_int4(-1, 0, 0, 0);
-        }
-        mbar_arrive_expect_tx(&full[s], (uint32_t)nvalid * R * HG * TR::ROW_BYTES * 2);
-      }
+      // K/V boxes first (the latency that matters), then the query tile and
+      // the bookkeeping; the tile's phase completes only at the arrive below.
+      if (lane == 0) mbar_expect_tx(&full[s], (uint32_t)nvalid * R * HG * TR::ROW_BYTES * 2);
       __syncwarp();
       uint8_t* st = stages + s * TR::STAGE_BYTES;
       for (int j = lane; j < nvalid; j += 32) {
@@ -367,15 +320,45 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
                            kv_policy);
         }
       }
+      if (lane == 0) {
+        if (first) {
+          mbar_arrive_expect_tx(&qfull[qs], qbytes);
+#pragma unroll
+          for (int sg = 0; sg < TR::NSEG; ++sg)
+            tma_load_3d(qtiles + qs * TR::Q_BYTES + sg * TR::QROWS * TR::SEGW, &p.tm_q, &qfull[qs],
+                        sg * (TR::SEGW / 2), c.hg * HG * G, c.b);
+        }
+        TileDesc dsc;
+        dsc.b = c.b;
+        dsc.hg = c.hg;
+        dsc.i = c.i;
+        dsc.seq = c.seq;
+        dsc.flags = (first ? kFirst : 0) | (last ? kLast : 0) | (split ? kSplit : 0);
+        // Partial slots: pair p uses slots [p + owner(start_p), ...], one per
+        // partition touching it; partition w writes slot p + w. These ranges
+        // are disjoint across pairs and stay below partitions + pairs.
+        dsc.slot = pair + w;
+        dsc.qslot = qs;
+        dsc.pad = 0;
+        descs[s] = dsc;
+        mbar_arrive(&full[s]);
+        // The partition holding a pair's first tile publishes its merge
+        // descriptor (indexed by pair or by partition, see meta_by_pair).
+        if (c.i == 0 && (split || p.meta_by_pair)) {
+          const int last_owner = part_owner((int64_t)c.pair_start + c.n - 1, total, W);
+          p.ws_meta[p.meta_by_pair ? pair : w] =
+              split ? make_int4(pair, pair + w, last_owner - w + 1, 1) : make_int4(-1, 0, 0, 0);
+        }
+      }
       if (k == 0 && lane == 0) PAD_STAMP(2);
       ++issued;
       if (first) ++segs;
       if (k + S < ntiles) {
         load_page_ids<TR>(p, la, lane, pend);
-        cursor_next<TR>(la, p, cap, ngroups, sseq);
+        cursor_next<TR>(la, p, cap, ngroups, sseq, useq);
         have_pend = true;
       }
-      cursor_next<TR>(c, p, cap, ngroups, sseq);
+      cursor_next<TR>(c, p, cap, ngroups, sseq, useq);
     }
     if (!ok) {
       // Unwind: record the failure, stop the consumers, and wait (bounded)
@@ -393,6 +376,85 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
   }
 
   // =============================== consumer warps ===============================
+  // ---- exclusive scan of tiles per sequence (x head groups) over the
+  // consumer threads: this partition's tile range, its first cursor (handed
+  // to the producer when it cannot use the fast start) and the seq_lens cache.
+  int t0, t1, ntiles;
+  {
+    const int per = (p.batch + kConsumerThreads - 1) / kConsumerThreads;
+    const int b_lo = min(p.batch, tid * per), b_hi = min(p.batch, b_lo + per);
+    int local = 0, bad = 0, any_empty = 0;
+    for (int b = b_lo; b < b_hi; ++b) {
+      const int raw = raw_seq(p, b);
+      bad |= (raw < 0 || raw > cap);
+      const int sq = clamp_seq(raw, cap);
+      if (b < kSeqCache) sseq[b] = sq;
+      any_empty |= (sq == 0);
+      local += tiles_of<TR>(sq);
+    }
+    local *= ngroups;
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) scan[warp] = incl;
+    any_empty = !named_barrier_and(2, kConsumerThreads, !any_empty);
+    int excl = incl - local, total = 0;
+#pragma unroll
+    for (int x = 0; x < kConsumerWarps; ++x) {
+      const int v = scan[x];
+      if (x < warp) excl += v;
+      total += v;
+    }
+    if (bad && w == 0) raise_flag(p, PAD_FLAG_SEQ_LEN_RANGE);
+    t0 = total > 0 ? part_begin(w, total, W) : 0;
+    t1 = total > 0 ? part_begin(w + 1, total, W) : 0;
+    if (t0 < total && excl <= t0 && t0 < excl + local) {
+      int acc_t = excl;
+      for (int b = b_lo; b < b_hi; ++b) {
+        const int seq = seq_of(p, sseq, b, cap);
+        const int n = tiles_of<TR>(seq);
+        const int tb = n * ngroups;
+        if (t0 < acc_t + tb) {
+          const int o = t0 - acc_t;
+          cur_smem[0] = b;
+          cur_smem[1] = o / n;
+          cur_smem[2] = o % n;
+          cur_smem[3] = n;
+          cur_smem[4] = seq;
+          cur_smem[5] = acc_t + (o / n) * n;
+          break;
+        }
+        acc_t += tb;
+      }
+    }
+    if (tid == 0) {
+      range_smem[0] = t0;
+      range_smem[1] = t1;
+      range_smem[2] = total;
+    }
+    named_barrier_arrive(3, kThreads);  // range, cursor and seq_lens cache to the producer
+    if (tid == 0) PAD_STAMP(1);
+    // the merge kernel may be scheduled now; it waits for this grid's results
+    if (tid == 0) pdl_launch_dependents();
+
+    // ---- zero output rows of empty sequences (src/reference.py:32-34)
+    // (only when the scan saw one: no extra global reads on the common path)
+    for (int b = w; any_empty && b < p.batch; b += (int)W) {
+      if (seq_of(p, sseq, b, cap) == 0) {
+        if (p.meta_by_pair && tid < ngroups) p.ws_meta[b * ngroups + tid] = make_int4(-1, 0, 0, 0);
+        const int hq = p.hkv * G;
+#pragma unroll 1
+        for (int x = tid; x < hq * (D / 2); x += kConsumerThreads) {
+          const int hh = x / (D / 2), d = (x % (D / 2)) * 2;
+          *reinterpret_cast<__half2*>(p.out + b * p.out_sb + hh * p.out_sh + d) = __floats2half2_rn(0.f, 0.f);
+        }
+      }
+    }
+  }
+  ntiles = t1 - t0;
   if (ntiles <= 0) return;
   const int hl = warp / WPH;               // local KV head this warp serves
   const uint32_t t_base = (warp % WPH) * 16;  // its 16 tokens within the tile
@@ -540,6 +602,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
 
+    if (k == ntiles - 1 && warp == 0 && lane == 0) PAD_STAMP(8);
     if (dsc.flags & kLast) {
       // ------------- segment epilogue: merge the WPH warps of each head, write
       // the fp16 output rows (pair finished here) or the fp32 partial (split pair)
@@ -666,6 +729,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
       }
     }
   }
+  if (warp == 0 && lane == 0) PAD_STAMP(9);
 }
 
 // Phase 2: merge the partials of one split (sequence, head group) pair for
@@ -690,10 +754,11 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const float* __res
   constexpr int PG = kMergeThreads / C4;   // partial groups folded in parallel
   __shared__ float red_o[PG][DC];
   __shared__ float red_m[PG], red_l[PG];
+  if (threadIdx.x == 0) PAD_MSTAMP(0);
   pdl_launch_dependents();  // the next decode may start its own set-up
   pdl_wait_primary();
   const int w = blockIdx.x, y = blockIdx.y, tid = threadIdx.x;
-  if (tid == 0) PAD_STAMP_MIN(0);
+  if (tid == 0) PAD_MSTAMP(1);
   const int4 meta = ws_meta[w];
   if (meta.w != 1) return;
   const int pair = meta.x, s0 = meta.y, ns = meta.z;
@@ -726,6 +791,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const float* __res
       m = mn;
     }
   }
+  if (tid == 0) PAD_MSTAMP(3);
   *reinterpret_cast<float4*>(&red_o[sg][(c - blockIdx.z * C4) * 4]) = a;
   if (tid % C4 == 0) {
     red_m[sg] = m;
@@ -754,7 +820,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const float* __res
     __half* o = out + b * out_sb + (int64_t)(hg * rows + y) * out_sh + blockIdx.z * DC + tid * 4;
     reinterpret_cast<__half2*>(o)[0] = __floats2half2_rn(t.x * inv, t.y * inv);
     reinterpret_cast<__half2*>(o)[1] = __floats2half2_rn(t.z * inv, t.w * inv);
-    if (tid == 0) PAD_STAMP_MAX(1);
+    if (tid == 0) PAD_MSTAMP(2);
   }
 }
 
