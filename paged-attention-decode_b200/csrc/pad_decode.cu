@@ -406,6 +406,7 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, const i
   prm.max_pages = (int)max_pages_per_seq;
   prm.box_rows = plan.box_rows;
   prm.box_rows_log2 = __builtin_ctz((unsigned)plan.box_rows);
+  prm.page_shift = (page_size & (page_size - 1)) == 0 ? __builtin_ctz((unsigned)page_size) : -1;
   prm.meta_by_pair = batch * (num_kv_heads / in.hg) < plan.partitions ? 1 : 0;
   prm.scale_log2 = scale * kLog2e;
 

@@ -61,6 +61,7 @@ struct __align__(64) DecodeParams {
   int batch, hkv, gqa, page_size, num_pages, max_pages;
   int box_rows;      // R: tokens per TMA box (a power of two dividing page_size and TT)
   int box_rows_log2; // log2(R)
+  int page_shift;    // log2(page_size) when it is a power of two, else -1
   int meta_by_pair;  // merge descriptors indexed by pair (else by partition)
   float scale_log2;  // scale * log2(e)
 };
@@ -91,7 +92,10 @@ struct Traits {
   // Cross-warp merge buffer (only when several warps share a head).
   // Two buffers (a two-level add tree) when 4 or more warps share a head.
   static constexpr int EPI_BUFS = WPH >= 4 ? 2 : 1;
-  static constexpr int EPI_BYTES = WPH > 1 ? EPI_BUFS * HG * 8 * NT * D * 4 : 0;
+  // Rows padded to D + 4 floats: the accumulator fragments' stores (lanes
+  // spread over 4 rows x 8 columns) then hit 32 distinct banks.
+  static constexpr int EPI_LD = D + 4;
+  static constexpr int EPI_BYTES = WPH > 1 ? EPI_BUFS * HG * 8 * NT * EPI_LD * 4 : 0;
   static constexpr int MISC_BYTES = 4096 + kSeqCache * 4;  // + cached seq_lens
   // Query tiles in flight: two (one segment ahead) unless that costs a stage.
   static constexpr int QSLOTS = (kSmemBudget - (1024 + 2 * Q_BYTES + EPI_BYTES + MISC_BYTES)) / STAGE_BYTES >= 3 ? 2 : 1;

@@ -81,20 +81,39 @@ __device__ __forceinline__ Cursor uniform_cursor(int t, int seq, int ngroups, in
   return Cursor{b, hg, i, n, seq, t - i, (int64_t)b * bt_stride};
 }
 
-// Page ids of the TMA boxes of the tile at cursor `c`: lane l loads boxes
-// l, l + 32, ... Boxes past seq_len get id 0 and are never issued. The loads
-// are pinned in program order so that they start as early as written.
+// Page holding token `tok` of a sequence, and the token's row in it (shift
+// and mask for power-of-two page sizes).
+__device__ __forceinline__ int page_of(const DecodeParams& p, int tok) {
+  return p.page_shift >= 0 ? tok >> p.page_shift : tok / p.page_size;
+}
+__device__ __forceinline__ int row_in_page(const DecodeParams& p, int tok) {
+  return p.page_shift >= 0 ? tok & (p.page_size - 1) : tok % p.page_size;
+}
+
+// Addresses of the page ids of the TMA boxes of the tile at cursor `c`: lane
+// l takes boxes l, l + 32, ... Boxes past seq_len get no address (id 0, never
+// issued).
 template <class TR>
-__device__ __forceinline__ void load_page_ids(const DecodeParams& p, const Cursor& c, int lane,
-                                              int (&dst)[TR::NB_PER_LANE]) {
+__device__ __forceinline__ void page_id_ptrs(const DecodeParams& p, const Cursor& c, int lane,
+                                             const int32_t* (&dst)[TR::NB_PER_LANE]) {
   const int R = p.box_rows;
-  const int64_t row = c.base;
 #pragma unroll
   for (int u = 0; u < TR::NB_PER_LANE; ++u) {
     const int j = lane + 32 * u;
     const int tok = c.i * TR::TT + j * R;
-    dst[u] = (j * R < TR::TT && tok < c.seq) ? ld_nc_early(p.block_table + row + tok / p.page_size) : 0;
+    dst[u] = (j * R < TR::TT && tok < c.seq) ? p.block_table + c.base + page_of(p, tok) : nullptr;
   }
+}
+
+// Page ids of the tile at cursor `c` (see page_id_ptrs). The loads are
+// pinned in program order so that they start as early as written.
+template <class TR>
+__device__ __forceinline__ void load_page_ids(const DecodeParams& p, const Cursor& c, int lane,
+                                              int (&dst)[TR::NB_PER_LANE]) {
+  const int32_t* a[TR::NB_PER_LANE];
+  page_id_ptrs<TR>(p, c, lane, a);
+#pragma unroll
+  for (int u = 0; u < TR::NB_PER_LANE; ++u) dst[u] = a[u] != nullptr ? ld_nc_early(a[u]) : 0;
 }
 
 template <class TR>
@@ -178,6 +197,25 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
   const int tg_total = (p.csr_indptr == nullptr && p.batch <= kFastBatch) ? p.batch * ngroups * ncap : 0;
   const int tg0 = tg_total > 0 ? part_begin(w, tg_total, W) : 0;
   const int tg1 = tg_total > 0 ? part_begin(w + 1, tg_total, W) : 0;
+  // the producer's guessed first cursor, the cursor S tiles on, and the
+  // addresses of the guessed tiles' page ids
+  Cursor gc{-1, 0, 0, 0, 0, 0, 0}, gla = gc;
+  const int32_t* gptr[S][TR::NB_PER_LANE];
+#pragma unroll
+  for (int k = 0; k < S; ++k)
+#pragma unroll
+    for (int u = 0; u < TR::NB_PER_LANE; ++u) gptr[k][u] = nullptr;
+  if (warp == kConsumerWarps && tg_total > 0) {
+    gc = uniform_cursor<TR>(tg0, cap, ngroups, p.bt_stride);
+    gla = gc;
+#pragma unroll
+    for (int k = 0; k < S; ++k) {
+      if (tg0 + k < tg1) {
+        page_id_ptrs<TR>(p, gla, lane, gptr[k]);
+        cursor_next<TR>(gla, p, cap, ngroups, sseq, cap);
+      }
+    }
+  }
 
   // Launched as a programmatic dependent of the previous kernel in the
   // stream: everything above touches only this CTA's shared memory; wait for
@@ -198,16 +236,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     Cursor c{-1, 0, 0, 0, 0, 0, 0};
     int pid[S][TR::NB_PER_LANE];
     if (tg_total > 0) {
-      {
-        Cursor g = uniform_cursor<TR>(tg0, cap, ngroups, p.bt_stride);
 #pragma unroll
-        for (int k = 0; k < S; ++k) {
-          if (tg0 + k < tg1) {
-            load_page_ids<TR>(p, g, lane, pid[k]);
-            cursor_next<TR>(g, p, cap, ngroups, sseq, cap);
-          }
-        }
-      }
+      for (int k = 0; k < S; ++k)
+#pragma unroll
+        for (int u = 0; u < TR::NB_PER_LANE; ++u) pid[k][u] = gptr[k][u] != nullptr ? ld_nc_early(gptr[k][u]) : 0;
       int mn = INT_MAX, mx = INT_MIN;
 #pragma unroll
       for (int u = 0; u < kFastBatch / 32; ++u) {
@@ -220,6 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
       }
       mn = __reduce_min_sync(0xffffffffu, mn);
       mx = __reduce_max_sync(0xffffffffu, mx);
+      if (lane == 0) PAD_STAMP(13);
       if (mn == mx && mn > 0 && mn <= cap) {
         useq = mn;
         if (mn == cap) {
@@ -227,12 +260,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
           t1 = tg1;
           total = tg_total;
           have_ids = true;
+          c = gc;
         } else {
           total = p.batch * ngroups * tiles_of<TR>(mn);
           t0 = part_begin(w, total, W);
           t1 = part_begin(w + 1, total, W);
+          if (t0 < total) c = uniform_cursor<TR>(t0, useq, ngroups, p.bt_stride);
         }
-        if (t0 < total) c = uniform_cursor<TR>(t0, useq, ngroups, p.bt_stride);
       }
     }
     if (useq >= 0) {
@@ -260,12 +294,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     }
     const int R = p.box_rows;
     const uint64_t kv_policy = l2_evict_first_policy();
-    Cursor la = c;
+    Cursor la = have_ids ? gla : c;
+    if (!have_ids) {
 #pragma unroll
-    for (int k = 0; k < S; ++k) {
-      if (k < ntiles) {
-        if (!have_ids) load_page_ids<TR>(p, la, lane, pid[k]);
-        cursor_next<TR>(la, p, cap, ngroups, sseq, useq);
+      for (int k = 0; k < S; ++k) {
+        if (k < ntiles) {
+          load_page_ids<TR>(p, la, lane, pid[k]);
+          cursor_next<TR>(la, p, cap, ngroups, sseq, useq);
+        }
       }
     }
     if (lane == 0) PAD_STAMP(5);
@@ -292,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
       __syncwarp();
       const int tok0 = c.i * TT;
       const int vt = min(TT, c.seq - tok0);
-      const int nvalid = (vt + R - 1) / R;
+      const int nvalid = (vt + R - 1) >> p.box_rows_log2;
       const bool first = (k == 0) || (c.i == 0);
       const bool last = (k == ntiles - 1) || (c.i == c.n - 1);
       const int pair = c.b * ngroups + c.hg;
@@ -307,15 +343,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
       // the bookkeeping; the tile's phase completes only at the arrive below.
       if (lane == 0) mbar_expect_tx(&full[s], (uint32_t)nvalid * R * HG * TR::ROW_BYTES * 2);
       __syncwarp();
+      if (k == 0 && lane == 0) PAD_STAMP(14);
       uint8_t* st = stages + s * TR::STAGE_BYTES;
       for (int j = lane; j < nvalid; j += 32) {
         const int page = ids[s * TR::NB_MAX + j];
         if ((unsigned)page >= (unsigned)p.num_pages) raise_flag(p, PAD_FLAG_BAD_PAGE_ID);
-        const int row = (tok0 + j * R) % p.page_size;
+        const int row = row_in_page(p, tok0 + j * R);
 #pragma unroll
         for (int sg = 0; sg < TR::NSEG; ++sg) {
           const int off = sg * kTileRows * TR::SEGW + j * (int)TR::box_pitch(R);
           tma_load_4d_hint(st + off, &p.tm_k, &full[s], sg * (TR::SEGW / 2), row, c.hg * HG, page, kv_policy);
+          if (k == 0 && j == 0 && sg == 0) PAD_STAMP(15);
           tma_load_4d_hint(st + TR::KT_BYTES + off, &p.tm_v, &full[s], sg * (TR::SEGW / 2), row, c.hg * HG, page,
                            kv_policy);
         }
@@ -649,6 +687,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
             for (int j = 0; j < 2; ++j) sml[warp * 8 * NT + nt * 8 + gl + j] = make_float2(m_run[nt][j], lsum[nt][j]);
         }
         consumer_sync();
+        if (k == ntiles - 1 && warp == 0 && lane == 0) PAD_STAMP(11);
         float scl[NT][2];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
@@ -671,9 +710,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
         // the WPH warps of a head add their rescaled O^T into EPI_BUFS buffers
         // in a fixed order (deterministic results): warp tb stores (first
         // step) or adds into buffer tb % EPI_BUFS at step tb / EPI_BUFS
-        constexpr int NB = TR::EPI_BUFS, BUF = HG * 8 * NT * D;
+        constexpr int NB = TR::EPI_BUFS, LD = TR::EPI_LD, BUF = HG * 8 * NT * LD;
         const int tb = (int)(t_base / 16);
-        float* buf = epi + (tb % NB) * BUF + hl * (8 * NT * D);
+        float* buf = epi + (tb % NB) * BUF + hl * (8 * NT * LD);
 #pragma unroll 1
         for (int step = 0; step < WPH / NB; ++step) {
           if (tb / NB == step) {
@@ -683,7 +722,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
               for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                  const int idx = (nt * 8 + gl + (e & 1)) * D + mt * 16 + (lane >> 2) + (e >= 2 ? 8 : 0);
+                  const int idx = (nt * 8 + gl + (e & 1)) * LD + mt * 16 + (lane >> 2) + (e >= 2 ? 8 : 0);
                   const float v = acc[mt][nt][e] * scl[nt][e & 1];
                   if (step == 0) buf[idx] = v;
                   else buf[idx] += v;
@@ -691,6 +730,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
           }
           consumer_sync();
         }
+        if (k == ntiles - 1 && warp == 0 && lane == 0) PAD_STAMP(12);
         const int ctid = warp * 32 + lane;
         if (!split) {
           __half* obase = p.out + dsc.b * p.out_sb + (int64_t)(dsc.hg * HG * G) * p.out_sh;
@@ -700,7 +740,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
             const int h = row / G, g = row % G;
             const float L = sML[h * 8 * NT + g].y;
             const float inv = L > 0.f ? 1.f / L : 0.f;
-            const float* src = epi + h * (8 * NT * D) + g * D + d;
+            const float* src = epi + h * (8 * NT * LD) + g * LD + d;
             float v0 = src[0], v1 = src[1];
             if constexpr (NB == 2) {
               v0 += src[BUF];
@@ -714,9 +754,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
           for (int x = ctid; x < HG * G * (D / 4); x += 32 * kConsumerWarps) {
             const int row = x / (D / 4), d = (x % (D / 4)) * 4;
             const int h = row / G, g = row % G;
-            float4 v = *reinterpret_cast<const float4*>(epi + h * (8 * NT * D) + g * D + d);
+            float4 v = *reinterpret_cast<const float4*>(epi + h * (8 * NT * LD) + g * LD + d);
             if constexpr (NB == 2) {
-              const float4 u = *reinterpret_cast<const float4*>(epi + BUF + h * (8 * NT * D) + g * D + d);
+              const float4 u = *reinterpret_cast<const float4*>(epi + BUF + h * (8 * NT * LD) + g * LD + d);
               v = make_float4(v.x + u.x, v.y + u.y, v.z + u.z, v.w + u.w);
             }
             o4[x] = v;
@@ -752,8 +792,10 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const float* __res
   constexpr int DC = D / DS;               // columns of D this CTA merges (blockIdx.z picks which)
   constexpr int C4 = DC / 4;               // float4 columns of one partial row slice
   constexpr int PG = kMergeThreads / C4;   // partial groups folded in parallel
-  __shared__ float red_o[PG][DC];
-  __shared__ float red_m[PG], red_l[PG];
+  constexpr int NW = kMergeThreads / 32;   // warps
+  static_assert(C4 <= 32 && 32 % C4 == 0, "a warp holds whole groups");
+  __shared__ float red_o[NW][DC];
+  __shared__ float red_m[NW], red_l[NW];
   if (threadIdx.x == 0) PAD_MSTAMP(0);
   pdl_launch_dependents();  // the next decode may start its own set-up
   pdl_wait_primary();
@@ -792,22 +834,44 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const float* __res
     }
   }
   if (tid == 0) PAD_MSTAMP(3);
-  *reinterpret_cast<float4*>(&red_o[sg][(c - blockIdx.z * C4) * 4]) = a;
-  if (tid % C4 == 0) {
-    red_m[sg] = m;
-    red_l[sg] = l;
+  // Fold the groups of one warp (lanes C4 apart hold the same columns) with
+  // shuffles, then the warps' states through shared memory.
+#pragma unroll
+  for (int o = C4; o < 32; o <<= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), l2 = __shfl_xor_sync(0xffffffffu, l, o);
+    float4 a2;
+    a2.x = __shfl_xor_sync(0xffffffffu, a.x, o);
+    a2.y = __shfl_xor_sync(0xffffffffu, a.y, o);
+    a2.z = __shfl_xor_sync(0xffffffffu, a.z, o);
+    a2.w = __shfl_xor_sync(0xffffffffu, a.w, o);
+    const float mn = fmaxf(m, m2), mu = (mn == -INFINITY) ? 0.f : mn;
+    const float al = ex2(m - mu), be = ex2(m2 - mu);
+    l = l * al + l2 * be;
+    a.x = a.x * al + a2.x * be;
+    a.y = a.y * al + a2.y * be;
+    a.z = a.z * al + a2.z * be;
+    a.w = a.w * al + a2.w * be;
+    m = mn;
+  }
+  const int wid = tid >> 5, lid = tid & 31;
+  if (lid < C4) {
+    *reinterpret_cast<float4*>(&red_o[wid][lid * 4]) = a;
+    if (lid == 0) {
+      red_m[wid] = m;
+      red_l[wid] = l;
+    }
   }
   __syncthreads();
   if (tid < C4) {
     float M = -INFINITY;
-#pragma unroll 8
-    for (int x = 0; x < PG; ++x) M = fmaxf(M, red_m[x]);
+#pragma unroll
+    for (int x = 0; x < NW; ++x) M = fmaxf(M, red_m[x]);
     const float Mu = (M == -INFINITY) ? 0.f : M;
     float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
     float L = 0.f;
-#pragma unroll 8
-    for (int x = 0; x < PG; ++x) {
-      const float wt = ex2(red_m[x] - Mu);  // 0 for groups that saw no partial
+#pragma unroll
+    for (int x = 0; x < NW; ++x) {
+      const float wt = ex2(red_m[x] - Mu);  // 0 for warps that saw no partial
       const float4 v = *reinterpret_cast<const float4*>(&red_o[x][tid * 4]);
       t.x += v.x * wt;
       t.y += v.y * wt;
