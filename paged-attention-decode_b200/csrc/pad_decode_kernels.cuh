@@ -309,23 +309,29 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     for (int k = 0; k < S; ++k)
       if (k < ntiles) store_page_ids<TR>(ids + k * TR::NB_MAX, lane, pid[k]);
     __syncwarp();
-    int pend[TR::NB_PER_LANE];
-    bool have_pend = false;
+#ifdef PAD_TRACE
+    uint64_t tr_pwait = 0, tr_pbusy = 0;
+#endif
     int issued = 0, segs = 0;
     bool ok = true;
     const uint32_t qbytes = (uint32_t)(HG * G * TR::ROW_BYTES);
     for (int k = 0; k < ntiles; ++k) {
       const int s = k % S;
+#ifdef PAD_TRACE
+      const uint64_t tr0 = globaltimer_ns();
+#endif
       if (k >= S) ok = mbar_wait_bounded(&empty[s], ((k / S) - 1) & 1, kWaitTimeoutNs);
+#ifdef PAD_TRACE
+      const uint64_t tr1 = globaltimer_ns();
+      tr_pwait += tr1 - tr0;
+#endif
       if (!__all_sync(0xffffffffu, ok) || *abort_flag) {
         ok = false;
         break;
       }
-      if (have_pend) {
-        store_page_ids<TR>(ids + ((k - 1) % S) * TR::NB_MAX, lane, pend);
-        have_pend = false;
-      }
-      __syncwarp();
+      // this tile's page ids: copied into its slot S tiles ago (one copy
+      // group per tile; each lane reads only the ids it copied)
+      if (k >= S) cp_async_wait_group<S - 1>();
       const int tok0 = c.i * TT;
       const int vt = min(TT, c.seq - tok0);
       const int nvalid = (vt + R - 1) >> p.box_rows_log2;
@@ -391,13 +397,30 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
       if (k == 0 && lane == 0) PAD_STAMP(2);
       ++issued;
       if (first) ++segs;
+      // page ids of tile k + S, straight into the slot this tile just freed
       if (k + S < ntiles) {
-        load_page_ids<TR>(p, la, lane, pend);
+        const int32_t* a[TR::NB_PER_LANE];
+        page_id_ptrs<TR>(p, la, lane, a);
+#pragma unroll
+        for (int u = 0; u < TR::NB_PER_LANE; ++u)
+          if (lane + 32 * u < TR::NB_MAX)
+            cp_async_4(ids + s * TR::NB_MAX + lane + 32 * u, a[u] != nullptr ? a[u] : p.block_table, a[u] != nullptr);
         cursor_next<TR>(la, p, cap, ngroups, sseq, useq);
-        have_pend = true;
       }
+      cp_async_commit();
       cursor_next<TR>(c, p, cap, ngroups, sseq, useq);
+#ifdef PAD_TRACE
+      tr_pbusy += globaltimer_ns() - tr1;
+#endif
     }
+#ifdef PAD_TRACE
+    if (lane == 0) {
+      g_pad_trace[blockIdx.x * 32 + 16] = tr_pwait;
+      g_pad_trace[blockIdx.x * 32 + 17] = tr_pbusy;
+      g_pad_trace[blockIdx.x * 32 + 18] = ntiles;
+    }
+#endif
+    cp_async_wait_all();
     if (!ok) {
       // Unwind: record the failure, stop the consumers, and wait (bounded)
       // for this CTA's own copies still in flight before exiting.
@@ -507,9 +530,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
   float m_run[NT][2], l_run[NT][2];
   int segs = 0;
 
+#ifdef PAD_TRACE
+  uint64_t tr_cwait = 0, tr_ccomp = 0;
+#endif
   for (int k = 0; k < ntiles; ++k) {
     const int s = k % S;
+#ifdef PAD_TRACE
+    const uint64_t tc0 = globaltimer_ns();
+#endif
     bool ok = mbar_wait_bounded(&full[s], (k / S) & 1, kWaitTimeoutNs);
+#ifdef PAD_TRACE
+    const uint64_t tc1 = globaltimer_ns();
+    tr_cwait += tc1 - tc0;
+#endif
     const TileDesc dsc = descs[s];
     if (ok && (dsc.flags & kFirst)) {
       const int qs = dsc.qslot;
@@ -639,6 +672,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
+#ifdef PAD_TRACE
+    tr_ccomp += globaltimer_ns() - tc1;
+#endif
 
     if (k == ntiles - 1 && warp == 0 && lane == 0) PAD_STAMP(8);
     if (dsc.flags & kLast) {
@@ -770,6 +806,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     }
   }
   if (warp == 0 && lane == 0) PAD_STAMP(9);
+#ifdef PAD_TRACE
+  if (warp == 0 && lane == 0) {
+    g_pad_trace[blockIdx.x * 32 + 19] = tr_cwait;
+    g_pad_trace[blockIdx.x * 32 + 20] = tr_ccomp;
+  }
+#endif
 }
 
 // Phase 2: merge the partials of one split (sequence, head group) pair for
