@@ -94,6 +94,17 @@ int head_group_for(int64_t hkv, int64_t gqa) {
   return 1;
 }
 
+// Merge variant by partials per split pair (partitions / pairs): up to
+// kMergeWide the 128-thread kernel (one CTA per query row); above it D is
+// split over CTAs, and above kMergeDeep each thread keeps 8 loads in flight.
+#ifndef PAD_MERGE_WIDE
+#define PAD_MERGE_WIDE 16
+#endif
+#ifndef PAD_MERGE_DEEP
+#define PAD_MERGE_DEEP 32
+#endif
+constexpr int64_t kMergeWide = PAD_MERGE_WIDE, kMergeDeep = PAD_MERGE_DEEP;
+
 bool pick_instance(int64_t head_dim, int64_t gqa, int hg, bool swz, Instance* out) {
   const bool nt1 = gqa <= 8;
   switch (head_dim) {
@@ -434,9 +445,12 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, const i
     const int4* a2 = prm.ws_meta;
     __half* a3 = prm.out;
     int ngroups = (int)(num_kv_heads / in.hg), rows = (int)(gqa * in.hg);
-    void* margs[] = {&a0, &a1, &a2, &a3, &prm.out_sb, &prm.out_sh, &ngroups, &rows};
+    // closed-form split descriptors for a dense batch of full rows (grid by pair)
+    int guess_ncap = 0, guess_parts = (int)plan.partitions;
+    if (prm.meta_by_pair && !csr) guess_ncap = (int)((max_pages_per_seq * page_size + in.tt - 1) / in.tt);
+    void* margs[] = {&a0, &a1, &a2, &a3, &prm.out_sb, &prm.out_sh, &ngroups, &rows, &guess_ncap, &guess_parts};
     cudaLaunchConfig_t cfg = {};
-    const bool wide = plan.partitions > 4 * batch * ngroups;
+    const bool wide = plan.partitions > kMergeWide * batch * ngroups;
     const int64_t merge_x = prm.meta_by_pair ? batch * ngroups : plan.partitions;
     cfg.gridDim = dim3((unsigned)merge_x, (unsigned)rows, wide ? (unsigned)in.merge_dsplit : 1u);
     // A split pair has about partitions / pairs partials: fold a handful with a
@@ -449,7 +463,7 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, const i
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const bool deep = plan.partitions > 16 * batch * ngroups;  // > 16 partials per pair: 8 loads in flight
+    const bool deep = plan.partitions > kMergeDeep * batch * ngroups;  // 8 loads in flight
     e = cudaLaunchKernelExC(&cfg, wide ? (deep ? in.merge_large : in.merge_mid) : in.merge_small, margs);
     if (e != cudaSuccess) return cuda_fail(e, "launching the merge kernel");
   }
