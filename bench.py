@@ -157,8 +157,9 @@ def make_pools(cfg, batch, seq_len, seq_lens, device, min_bytes):
     return pools, per
 
 
-def time_device(pools, steps, warmup, torch, barrier):
-    """Device time of `steps` decode calls rotated over `pools` (ms)."""
+def time_device(pools, steps, warmup, torch, barrier, fn=None):
+    """Device time of `steps` decode calls rotated over `pools` (ms). `fn(case)`
+    replaces the call of this package (used for the same-box comparator)."""
     import pad_b200
 
     stream = torch.cuda.Stream()
@@ -166,6 +167,9 @@ def time_device(pools, steps, warmup, torch, barrier):
 
     def call(i):
         c = pools[i % len(pools)]
+        if fn is not None:
+            fn(c)
+            return
         pad_b200.paged_attention_decode_cuda_v4(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens,
                                                 out=outs[i % len(pools)])
 
@@ -260,6 +264,42 @@ def time_e2e_resident(pool, steps, torch):
     torch.cuda.synchronize()
     return s.elapsed_time(e) / steps, sum(t.numel() * t.element_size() for t in host), \
         out_h.numel() * out_h.element_size()
+
+
+def reference_gpu_comparator(torch, barrier, peak_gbs):
+    """The reference's own GPU kernel timed on this box the same way (CUDA-graph
+    replay over KV pools rotated past L2): its Triton v4 split-K kernel
+    (src/kernel_v4_split_k.py:213, num_splits=16), imported from the offline
+    install of the reference in baseline/_ref. Recorded beside our numbers,
+    not a target. Its CUDA v4 kernel is not in that install (the package
+    carries no .cu sources), so it cannot be built here."""
+    ref_dir = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
+    if not os.path.isfile(os.path.join(ref_dir, "kernel_v4_split_k.py")):
+        return {"unavailable": "baseline/_ref (offline install of the reference) is absent"}
+    sys.path.insert(0, ref_dir)
+    try:
+        import kernel_v4_split_k as ref_tv4
+    except Exception as e:  # noqa: BLE001 -- report, do not fail the bench
+        return {"unavailable": f"importing the reference Triton v4 failed: {e!r}"[:200]}
+    finally:
+        sys.path.remove(ref_dir)
+    import pad_b200
+
+    def fn(c):
+        return ref_tv4.paged_attention_decode_v4(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens, num_splits=16)
+
+    res = {"impl": "reference Triton v4 (src/kernel_v4_split_k.py, num_splits=16), same box and timing method"}
+    for cfg, b, sl in (("c2", 1, 4096), ("c2", 64, 4096), ("c3", 1, 32768)):
+        pl, nb = make_pools(cfg, b, sl, None, "cuda", 2.5 * L2_BYTES)
+        c = pl[0]
+        ours = pad_b200.paged_attention_decode_cuda_v4(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens)
+        diff = (fn(c).float() - ours.float()).abs().max().item()
+        m = time_device(pl, 200, 5, torch, barrier, fn=fn) / 200
+        res[f"{cfg}_batch{b}_seq{sl}"] = {"us_per_call": round(m * 1e3, 3), "TB_s": round(nb / (m * 1e-3) / 1e12, 4),
+                                         "frac_of_measured_hbm": round(nb / (m * 1e-3) / 1e9 / peak_gbs, 4),
+                                         "max_abs_diff_vs_ours": diff}
+        del pl
+    return res
 
 
 def cpu_baseline_sample(pool, seconds: float = 10.0):
@@ -397,6 +437,7 @@ def run_ours(args):
                             "frac_of_measured_hbm": round(nb / (m * 1e-3) / 1e9 / peak_gbs, 4)}
             del pl
         extra["long_context_c3_batch1"] = lc
+        extra["same_box_reference_gpu"] = reference_gpu_comparator(torch, barrier, peak_gbs)
 
     if rank == 0:
         line = {
