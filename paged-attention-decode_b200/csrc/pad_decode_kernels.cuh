@@ -716,15 +716,35 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
               }
           }
       } else {
+        // The WPH warps of a head merge their O^T into EPI_BUFS buffers in a
+        // fixed order (deterministic results). Warp tb of the head writes
+        // buffer tb % EPI_BUFS at step tb / EPI_BUFS: step 0 stores its
+        // accumulator unscaled, beside every warp's (m, l); step 1 rescales
+        // that content to the head's running max and adds its own; later
+        // steps add. One barrier fewer than exchanging (m, l) first.
+        constexpr int NB = TR::EPI_BUFS, LD = TR::EPI_LD, BUF = HG * 8 * NT * LD;
+        static_assert(WPH / NB >= 2, "every buffer gets a rescaling add");
+        const int tb = (int)(t_base / 16);
+        float* buf = epi + (tb % NB) * BUF + hl * (8 * NT * LD);
         if ((lane >> 2) == 0) {
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int j = 0; j < 2; ++j) sml[warp * 8 * NT + nt * 8 + gl + j] = make_float2(m_run[nt][j], lsum[nt][j]);
         }
+        if (tb < NB) {
+#pragma unroll
+          for (int mt = 0; mt < KSTEPS; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                buf[(nt * 8 + gl + (e & 1)) * LD + mt * 16 + (lane >> 2) + (e >= 2 ? 8 : 0)] = acc[mt][nt][e];
+        }
         consumer_sync();
         if (k == ntiles - 1 && warp == 0 && lane == 0) PAD_STAMP(11);
-        float scl[NT][2];
+        // scale of this warp's rows, and of the warp that stored this buffer
+        float scl[NT][2], s0[NT][2];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -734,23 +754,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
 #pragma unroll
             for (int ww = 0; ww < WPH; ++ww) M = fmaxf(M, sml[(hl * WPH + ww) * 8 * NT + g].x);
             const float Mu = (M == -INFINITY) ? 0.f : M;
-            float L = 0.f;
-#pragma unroll
-            for (int ww = 0; ww < WPH; ++ww) {
-              const float2 x = sml[(hl * WPH + ww) * 8 * NT + g];
-              L += x.y * ex2(x.x - Mu);
-            }
             scl[nt][j] = ex2(m_run[nt][j] - Mu);
-            if (t_base == 0 && (lane >> 2) == 0) sML[hl * 8 * NT + g] = make_float2(Mu, L);
+            s0[nt][j] = ex2(sml[(hl * WPH + tb % NB) * 8 * NT + g].x - Mu);
+            if (t_base == 0 && (lane >> 2) == 0) {
+              float L = 0.f;
+#pragma unroll
+              for (int ww = 0; ww < WPH; ++ww) {
+                const float2 x = sml[(hl * WPH + ww) * 8 * NT + g];
+                L += x.y * ex2(x.x - Mu);
+              }
+              sML[hl * 8 * NT + g] = make_float2(Mu, L);
+            }
           }
-        // the WPH warps of a head add their rescaled O^T into EPI_BUFS buffers
-        // in a fixed order (deterministic results): warp tb stores (first
-        // step) or adds into buffer tb % EPI_BUFS at step tb / EPI_BUFS
-        constexpr int NB = TR::EPI_BUFS, LD = TR::EPI_LD, BUF = HG * 8 * NT * LD;
-        const int tb = (int)(t_base / 16);
-        float* buf = epi + (tb % NB) * BUF + hl * (8 * NT * LD);
 #pragma unroll 1
-        for (int step = 0; step < WPH / NB; ++step) {
+        for (int step = 1; step < WPH / NB; ++step) {
           if (tb / NB == step) {
 #pragma unroll
             for (int mt = 0; mt < KSTEPS; ++mt)
@@ -760,7 +777,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
                 for (int e = 0; e < 4; ++e) {
                   const int idx = (nt * 8 + gl + (e & 1)) * LD + mt * 16 + (lane >> 2) + (e >= 2 ? 8 : 0);
                   const float v = acc[mt][nt][e] * scl[nt][e & 1];
-                  if (step == 0) buf[idx] = v;
+                  if (step == 1) buf[idx] = buf[idx] * s0[nt][e & 1] + v;
                   else buf[idx] += v;
                 }
           }
