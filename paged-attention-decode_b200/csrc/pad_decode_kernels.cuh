@@ -14,7 +14,14 @@ __device__ __forceinline__ void raise_flag(const DecodeParams& p, int bits) {
 }
 
 #ifdef PAD_TRACE
-// Development-only timeline: per-CTA %globaltimer stamps (compile with -DPAD_TRACE).
+// Development-only timeline: per-CTA %globaltimer stamps (compile with -DPAD_TRACE;
+// read back with pad_debug_trace_read). Decode slots: 0 start, 10 dependency
+// wait done, 13 seq_lens reduced (fast start), 7 producer ready, 5 first page
+// ids ready, 14 first expect_tx, 15 first K/V TMA instruction, 2 first tile
+// issued, 1 consumer scan done, 3 first tile ready, 4 last tile ready, 8 last
+// tile computed, 11 / 12 epilogue barrier / add tree done, 9 consumer exit;
+// 16-20 sums per CTA: producer wait and busy time, tiles, consumer (warp 0)
+// wait and compute time. Merge slots: 0 start, 1 wait done, 3 folded, 2 end.
 // Decode CTAs own 32 slots each; merge CTAs own 4 slots each after them.
 __device__ uint64_t g_pad_trace[1024 * 32 + 4096 * 4];
 #define PAD_STAMP(i) (g_pad_trace[blockIdx.x * 32 + (i)] = globaltimer_ns())
@@ -524,7 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
   // this lane's ldmatrix rows: K (A operand of S^T) and V (A operand of O^T)
   uint32_t k_row, k_sw, v_row, v_sw;
   TR::kv_row(t_base + (lane & 7) + ((lane >> 3) & 1) * 8, hl, lr, k_row, k_sw);
-  TR::kv_row(t_base + (lane & 7) + ((lane >> 4) & 1) * 8, hl, lr, v_row, v_sw);            // first query row (within an n8 tile) this lane owns
+  TR::kv_row(t_base + (lane & 7) + ((lane >> 4) & 1) * 8, hl, lr, v_row, v_sw);
   uint32_t qf[KSTEPS][NT][2];
   float acc[KSTEPS][NT][4];
   float m_run[NT][2], l_run[NT][2];
