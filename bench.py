@@ -302,6 +302,54 @@ def reference_gpu_comparator(torch, barrier, peak_gbs):
     return res
 
 
+def flashinfer_comparator(torch, barrier, peak_gbs):
+    """FlashInfer's paged decode (BatchDecodeWithPagedKVCacheWrapper, tensor
+    cores, the configuration the reference's own adapter uses,
+    src/flashinfer_adapter.py:92-107) on this box: planned once per KV pool
+    with CUDA-graph buffers, then timed exactly like our kernel. A library
+    comparator, recorded beside our numbers; never on our path."""
+    try:
+        import flashinfer
+    except Exception as e:  # noqa: BLE001 -- report, do not fail the bench
+        return {"unavailable": f"import flashinfer failed: {e!r}"[:200]}
+    import pad_b200
+    from pad_b200 import paged_kv_indices
+
+    res = {"impl": f"flashinfer {getattr(flashinfer, '__version__', '?')} BatchDecodeWithPagedKVCacheWrapper "
+                   "(NHD, use_tensor_cores=True, CUDA-graph buffers), same box and timing method"}
+    try:
+        for cfg, b, sl in (("c2", 1, 4096), ("c2", 64, 4096), ("c3", 1, 32768)):
+            pl, nb = make_pools(cfg, b, sl, None, "cuda", 2.5 * L2_BYTES)
+            c = pl[0]
+            _, hq, d = c.q.shape
+            _, ps, hkv, _ = c.k_cache.shape
+            wraps = {}
+            for cc in pl:
+                ip, ix, lp = paged_kv_indices(cc.block_table, cc.seq_lens, ps)
+                ws = torch.zeros(128 << 20, dtype=torch.uint8, device="cuda")
+                wr = flashinfer.BatchDecodeWithPagedKVCacheWrapper(
+                    ws, "NHD", use_cuda_graph=True, use_tensor_cores=True, paged_kv_indptr_buffer=ip.clone(),
+                    paged_kv_indices_buffer=ix.clone(), paged_kv_last_page_len_buffer=lp.clone())
+                wr.plan(ip, ix, lp, hq, hkv, d, ps, q_data_type=torch.float16, sm_scale=d ** -0.5)
+                wraps[id(cc)] = (wr, torch.empty_like(cc.q))
+
+            def fn(cc):
+                wr, o = wraps[id(cc)]
+                return wr.run(cc.q, (cc.k_cache, cc.v_cache), out=o)
+
+            ours = pad_b200.paged_attention_decode_cuda_v4(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens)
+            diff = (fn(c).float() - ours.float()).abs().max().item()
+            m = time_device(pl, 200, 5, torch, barrier, fn=fn) / 200
+            res[f"{cfg}_batch{b}_seq{sl}"] = {"us_per_call": round(m * 1e3, 3),
+                                             "TB_s": round(nb / (m * 1e-3) / 1e12, 4),
+                                             "frac_of_measured_hbm": round(nb / (m * 1e-3) / 1e9 / peak_gbs, 4),
+                                             "max_abs_diff_vs_ours": diff}
+            del pl, wraps
+    except Exception as e:  # noqa: BLE001
+        res["unavailable"] = f"flashinfer run failed: {e!r}"[:200]
+    return res
+
+
 def cpu_baseline_sample(pool, seconds: float = 10.0):
     """The C oracle (oracle/pa_oracle.c, the reference algorithm) on the host
     cores, on a bounded sample of the workload's sequences; TB/s of KV read."""
@@ -438,6 +486,7 @@ def run_ours(args):
             del pl
         extra["long_context_c3_batch1"] = lc
         extra["same_box_reference_gpu"] = reference_gpu_comparator(torch, barrier, peak_gbs)
+        extra["same_box_flashinfer"] = flashinfer_comparator(torch, barrier, peak_gbs)
 
     if rank == 0:
         line = {
