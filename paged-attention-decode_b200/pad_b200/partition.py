@@ -78,10 +78,19 @@ def plan(seq_lens, num_groups: int, parts: int, cap: int | None = None, tt: int 
     return total, pairs
 
 
+FEW_PAIRS = 16
+
+
 def heuristic_partitions(num_sms: int, ctas_per_sm: int, batch: int, num_kv_heads: int, gqa_ratio: int,
                          max_pages: int, page_size: int) -> int:
-    """The num_splits=None choice: one partition per resident CTA slot,
-    capped by the number of tiles the batch can hold."""
+    """The num_splits=None choice: one partition per resident CTA slot --
+    rounded down to a power of two when there are at most FEW_PAIRS
+    (sequence, head group) pairs -- capped by the number of tiles the batch
+    can hold."""
     hg = head_group(num_kv_heads, gqa_ratio)
-    cap_tiles = batch * (num_kv_heads // hg) * tiles_of(max_pages * page_size, TILE_ROWS // hg)
-    return max(1, min(num_sms * ctas_per_sm, cap_tiles))
+    groups = num_kv_heads // hg
+    cap_tiles = batch * groups * tiles_of(max_pages * page_size, TILE_ROWS // hg)
+    parts = num_sms * ctas_per_sm
+    if batch * groups <= FEW_PAIRS:
+        parts = 1 << (parts.bit_length() - 1)
+    return max(1, min(parts, cap_tiles))

@@ -114,5 +114,11 @@ def test_partition_covers_every_tile_once_with_disjoint_slots(seed, parts):
 def test_heuristic_partitions():
     assert partition.heuristic_partitions(148, 1, 64, 2, 6, 256, 16) == 148
     assert partition.heuristic_partitions(148, 1, 1, 2, 6, 1, 16) == 1  # tiny batch: one per tile
+    # at most 16 (sequence, head group) pairs: a power-of-two partition count
+    assert partition.heuristic_partitions(148, 1, 1, 2, 6, 1024, 32) == 128   # C3 batch 1, 32k
+    assert partition.heuristic_partitions(148, 1, 16, 2, 6, 256, 16) == 128   # C2 batch 16
+    assert partition.heuristic_partitions(148, 1, 17, 2, 6, 256, 16) == 148   # 17 pairs: all CTAs
+    assert partition.heuristic_partitions(148, 1, 4, 8, 4, 512, 16) == 128    # 4 seqs x 1 group of 8 heads
+    assert partition.heuristic_partitions(148, 1, 2, 2, 6, 64, 16) == 32      # capped by tiles (2 x 16)
     assert partition.head_group(8, 4) == 8 and partition.head_group(2, 6) == 2 and partition.head_group(6, 1) == 2
     assert partition.head_group(8, 16) == 4 and partition.head_group(3, 2) == 1
