@@ -73,7 +73,10 @@ int pad_device_info(int device, int64_t head_dim, int64_t gqa_ratio, int* num_sm
  * launch for this problem on `device`.
  *   num_splits <= 0 : heuristic -- one partition per resident CTA slot
  *                     (num_sms * ctas_per_sm), capped by the number of
- *                     64-token tiles the batch can hold;
+ *                     tiles the batch can hold (a tile is 128 (token,
+ *                     KV head) rows: 128 / HG tokens of HG KV heads, HG the
+ *                     largest of 8, 4, 2, 1 dividing num_kv_heads, at most
+ *                     4 when gqa_ratio > 8);
  *   num_splits >= 1 : num_splits partitions per (sequence, KV head) pair,
  *                     i.e. num_splits * batch * num_kv_heads partitions. */
 int pad_decode_partitions(int device, int64_t batch, int64_t num_kv_heads, int64_t gqa_ratio,
@@ -103,6 +106,18 @@ int pad_decode_workspace_bytes(int device, int64_t batch, int64_t num_kv_heads, 
  * out_strides[3]; block_table_stride is the row stride of block_table.
  * error_flags (device int32, optional) receives PAD_FLAG_* bits; it is
  * OR-ed into, never cleared.
+ *
+ * Invalid values are flagged, never faulted on: a block_table entry outside
+ * [0, num_pages) sets PAD_FLAG_BAD_PAGE_ID and the tokens it addresses are
+ * read as zero K/V rows (the tensor copy zero-fills out-of-range boxes); a
+ * seq_len outside [0, max_pages_per_seq * page_size] sets
+ * PAD_FLAG_SEQ_LEN_RANGE and is clamped into that range. When either flag is
+ * set the output of the call is undefined (the reference oracle raises
+ * ValueError instead, src/reference.py:40-41,107-112).
+ *
+ * The library caches per-device facts (kernel attributes, occupancy, the
+ * no-alloc scratch address) for the life of the process; it must not be used
+ * across a cudaDeviceReset of a device it has run on.
  */
 int pad_paged_attention_decode(const void* q, const void* k_cache, const void* v_cache,
                                const int32_t* block_table, const int32_t* seq_lens, void* out,

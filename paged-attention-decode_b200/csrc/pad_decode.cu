@@ -7,35 +7,17 @@
 
 #include <algorithm>
 #include <cmath>
-#include <cstdarg>
-#include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <string>
 
 #include "pad_b200.h"
 #include "pad_decode_kernels.cuh"
+#include "pad_error.cuh"
 
 namespace {
 
 using namespace pad;
-
-thread_local std::string g_last_error;
-
-int fail(int status, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
-int fail(int status, const char* fmt, ...) {
-  char buf[512];
-  va_list ap;
-  va_start(ap, fmt);
-  vsnprintf(buf, sizeof(buf), fmt, ap);
-  va_end(ap);
-  g_last_error = buf;
-  return status;
-}
-
-int cuda_fail(cudaError_t e, const char* what) {
-  return fail(PAD_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
-}
 
 // ----------------------------------------------------------------- instances
 struct Instance {
@@ -289,7 +271,7 @@ const char* pad_status_string(int status) {
   }
 }
 
-const char* pad_last_error(void) { return g_last_error.c_str(); }
+const char* pad_last_error(void) { return pad::g_last_error.c_str(); }
 
 int pad_version(void) { return 100; }
 
@@ -332,7 +314,8 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, const i
                 int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t num_pages, int64_t page_size,
                 int64_t max_pages_per_seq, const int64_t* q_strides, const int64_t* k_strides,
                 const int64_t* v_strides, int64_t block_table_stride, const int64_t* out_strides, float scale,
-                int64_t num_splits, void* workspace, size_t workspace_bytes, void* stream, int32_t* error_flags) {
+                int64_t num_splits, void* workspace, size_t workspace_bytes, void* stream, int32_t* error_flags,
+                bool static_scratch = false) {
   const bool csr = csr_indptr != nullptr;
   // ---- shape-only checks (no device access, no sync)
   if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || num_pages < 0 || page_size <= 0 ||
@@ -380,6 +363,11 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, const i
   Plan plan;
   int st = make_plan(device, batch, num_kv_heads, gqa, head_dim, page_size, max_pages_per_seq, num_splits, &plan, csr);
   if (st != PAD_OK) return st;
+  if (static_scratch && plan.bytes > workspace_bytes)
+    return fail(PAD_ERR_WORKSPACE,
+                "problem needs %zu bytes of scratch, more than the %zu-byte static scratch of the no-alloc "
+                "entry point; use pad_paged_attention_decode with a caller-provided workspace",
+                plan.bytes, workspace_bytes);
   if (workspace == nullptr || workspace_bytes < plan.bytes)
     return fail(PAD_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", plan.bytes,
                 workspace == nullptr ? (size_t)0 : workspace_bytes);
@@ -555,22 +543,13 @@ int pad_paged_attention_decode_noalloc(const void* q, const void* k_cache, const
     }
     ptr = scratch_ptr[device];
   }
-  if (batch > 0 && num_q_heads > 0 && num_kv_heads > 0 && num_q_heads % num_kv_heads == 0 && num_pages > 0 &&
-      max_pages_per_seq > 0) {
-    size_t need = 0;
-    const int st = pad_decode_workspace_bytes(device, batch, num_kv_heads, num_q_heads / num_kv_heads, head_dim,
-                                              page_size, max_pages_per_seq, num_splits, &need);
-    if (st != PAD_OK) return st;
-    if (need > PAD_STATIC_SCRATCH_BYTES)
-      return fail(PAD_ERR_WORKSPACE,
-                  "problem needs %zu bytes of scratch, more than the %zu-byte static scratch of the no-alloc "
-                  "entry point; use pad_paged_attention_decode with a caller-provided workspace",
-                  need, (size_t)PAD_STATIC_SCRATCH_BYTES);
-  }
-  return pad_paged_attention_decode(q, k_cache, v_cache, block_table, seq_lens, out, batch, num_q_heads,
-                                    num_kv_heads, head_dim, num_pages, page_size, max_pages_per_seq, q_strides,
-                                    k_strides, v_strides, block_table_stride, out_strides, scale, num_splits, ptr,
-                                    PAD_STATIC_SCRATCH_BYTES, stream, error_flags);
+  // The size check against the scratch happens inside decode_impl, after the
+  // same argument checks as the workspace entry point (same status codes for
+  // bad arguments).
+  return decode_impl(q, k_cache, v_cache, block_table, seq_lens, nullptr, nullptr, out, batch, num_q_heads,
+                     num_kv_heads, head_dim, num_pages, page_size, max_pages_per_seq, q_strides, k_strides, v_strides,
+                     block_table_stride, out_strides, scale, num_splits, ptr, PAD_STATIC_SCRATCH_BYTES, stream,
+                     error_flags, /*static_scratch=*/true);
 }
 
 #ifdef PAD_TRACE

@@ -661,20 +661,32 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
           }
         }
       }
-      // P^T as the B operand: fp16 pack, then transpose 8x8 blocks in registers
-      uint32_t pb[NT][2];
+      // P^T as the B operand, split into two fp16 terms P = P_hi + P_lo
+      // (P_hi = fp16(P), P_lo = fp16(P - P_hi)), each transposed 8x8-blockwise
+      // in registers. Two MMAs per k-step then give O with P at ~22 bits, so
+      // O's numerator matches the fp32 l it is divided by; a single fp16 P
+      // alone leaves relative errors near 1e-2 on small outputs.
+      uint32_t pb[NT][2], pl[NT][2];
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        pb[nt][0] = movmatrix_trans(pack_half2(sc[nt][0], sc[nt][1]));
-        pb[nt][1] = movmatrix_trans(pack_half2(sc[nt][2], sc[nt][3]));
-      }
-      // O^T[D x 8*NT] += V^T[D x 16 tokens] . P^T
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float x0 = sc[nt][2 * h], x1 = sc[nt][2 * h + 1];
+          const __half2 hi = __floats2half2_rn(x0, x1);
+          const float2 hf = __half22float2(hi);
+          pb[nt][h] = movmatrix_trans(*reinterpret_cast<const uint32_t*>(&hi));
+          pl[nt][h] = movmatrix_trans(pack_half2(x0 - hf.x, x1 - hf.y));
+        }
+      // O^T[D x 8*NT] += V^T[D x 16 tokens] . (P_hi^T + P_lo^T)
 #pragma unroll
       for (int mt = 0; mt < KSTEPS; ++mt) {
         uint32_t a0, a1, a2, a3;
         ldsm_x4_trans(TR::kv_at(vb, v_row, v_sw, mt * 2 + ((lane >> 3) & 1)), a0, a1, a2, a3);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma_16816(acc[mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+        for (int nt = 0; nt < NT; ++nt) {
+          mma_16816(acc[mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+          mma_16816(acc[mt][nt], a0, a1, a2, a3, pl[nt][0], pl[nt][1]);
+        }
       }
     }
     __syncwarp();

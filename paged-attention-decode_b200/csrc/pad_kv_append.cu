@@ -13,6 +13,7 @@
 #include <cstdint>
 
 #include "pad_b200.h"
+#include "pad_error.cuh"
 
 namespace {
 
@@ -69,16 +70,20 @@ extern "C" int pad_paged_kv_append(const void* k_new, const void* v_new, void* k
                                    int64_t max_pages_per_seq, const int64_t* k_new_strides,
                                    const int64_t* v_new_strides, const int64_t* k_strides, const int64_t* v_strides,
                                    int64_t block_table_stride, void* stream, int32_t* error_flags) {
+  using pad::fail;
   if (batch < 0 || num_kv_heads <= 0 || head_dim <= 0 || num_pages < 0 || page_size <= 0 || max_pages_per_seq < 0)
-    return PAD_ERR_INVALID_ARGUMENT;
+    return fail(PAD_ERR_INVALID_ARGUMENT, "kv_append: negative or zero size");
   if (batch == 0 || num_pages == 0 || max_pages_per_seq == 0) return PAD_OK;
   if (k_new == nullptr || v_new == nullptr || k_cache == nullptr || v_cache == nullptr || block_table == nullptr ||
       positions == nullptr || k_new_strides == nullptr || v_new_strides == nullptr || k_strides == nullptr ||
       v_strides == nullptr)
-    return PAD_ERR_INVALID_ARGUMENT;
+    return fail(PAD_ERR_INVALID_ARGUMENT, "kv_append: null pointer argument");
+  if (block_table_stride < max_pages_per_seq)
+    return fail(PAD_ERR_INVALID_ARGUMENT, "kv_append: block_table row stride smaller than its width");
   if (k_new_strides[2] != 1 || v_new_strides[2] != 1 || k_strides[3] != 1 || v_strides[3] != 1)
-    return PAD_ERR_UNSUPPORTED;
-  if (batch * num_kv_heads > INT32_MAX || num_pages > INT32_MAX) return PAD_ERR_UNSUPPORTED;
+    return fail(PAD_ERR_UNSUPPORTED, "kv_append: the head_dim axis of every tensor must be contiguous");
+  if (batch * num_kv_heads > INT32_MAX || num_pages > INT32_MAX)
+    return fail(PAD_ERR_UNSUPPORTED, "kv_append: batch * num_kv_heads or num_pages exceeds int32");
   const bool vec = head_dim % 8 == 0 && al16(k_new) && al16(v_new) && al16(k_cache) && al16(v_cache) &&
                    k_new_strides[0] % 8 == 0 && k_new_strides[1] % 8 == 0 && v_new_strides[0] % 8 == 0 &&
                    v_new_strides[1] % 8 == 0 && k_strides[0] % 8 == 0 && k_strides[1] % 8 == 0 &&
@@ -92,5 +97,8 @@ extern "C" int pad_paged_kv_append(const void* k_new, const void* v_new, void* k
       (int)num_pages, (int)page_size, (int)max_pages_per_seq, k_new_strides[0], k_new_strides[1], v_new_strides[0],
       v_new_strides[1], k_strides[0], k_strides[1], k_strides[2], v_strides[0], v_strides[1], v_strides[2],
       block_table_stride, vec ? 1 : 0, error_flags);
-  return cudaGetLastError() == cudaSuccess ? PAD_OK : PAD_ERR_CUDA;
+  // the launch's own error only: cudaPeekAtLastError would also report (and
+  // cudaGetLastError clear) a sticky error left by unrelated earlier work
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PAD_OK : pad::cuda_fail(e, "launching the kv_append kernel");
 }

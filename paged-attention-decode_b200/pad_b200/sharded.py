@@ -4,12 +4,25 @@ Sequences are independent, so the batch is split into contiguous shards of
 sequences, one per rank; each rank owns the KV pages of its own sequences in a
 local page pool and runs the single-GPU decode on them. Nothing crosses
 NVLink on the hot path; the only collective is an optional gather of the
-outputs to rank 0 (for checking), done outside the decode.
+outputs to rank 0 (for checking), done after the decode.
 
 The reference has no multi-GPU code; this module adds the launcher the
-decode path needs to scale out (batch sharding, local page pools, output
-gather), written against ``torch.distributed`` so that the same logic runs on
-NCCL over NVLink and, for tests, on gloo over CPU processes.
+decode path needs to scale out, written against ``torch.distributed`` so that
+the same logic runs on NCCL over NVLink and, for tests, on gloo over CPU
+processes:
+
+* ``shard_range``     -- which sequences a rank owns;
+* ``LocalShard``      -- a rank's own problem: its q rows, its local page pool
+                         and its block table in local page ids;
+* ``localize``        -- cut a rank's shard out of a global problem (only that
+                         rank's pages are copied to its device);
+* ``ShardedDecoder``  -- the launcher: decode a rank's local shard on its GPU
+                         (the same call on every rank, no collective) and,
+                         optionally, gather the outputs to rank 0;
+* ``decode_sharded``  -- ``localize`` + ``ShardedDecoder`` for a global problem.
+
+A serving engine already holds each rank's pool on that rank; it builds a
+``LocalShard`` from its own tensors and calls ``ShardedDecoder.decode``.
 """
 
 from __future__ import annotations
@@ -29,6 +42,9 @@ def shard_range(batch: int, world: int, rank: int) -> tuple[int, int]:
 
 @dataclass
 class LocalShard:
+    """One rank's decode problem: sequences [lo, hi) of the global batch,
+    their KV pages in a local pool, block_table in local page ids."""
+
     lo: int
     hi: int
     q: torch.Tensor
@@ -36,49 +52,56 @@ class LocalShard:
     v_cache: torch.Tensor
     block_table: torch.Tensor
     seq_lens: torch.Tensor
-    page_map: torch.Tensor  # global page id of each local page
+    page_map: torch.Tensor | None = None  # global page id of each local page (None: built locally)
+
+
+def _as_tensor(a):
+    return a if isinstance(a, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(a))
 
 
 def localize(q, k_cache, v_cache, block_table, seq_lens, world: int, rank: int, device=None,
              shuffle_seed: int | None = None) -> LocalShard:
     """Cut rank `rank`'s sequences out of a global problem.
 
-    The pages its sequences reference (block_table[b, :ceil(seq_b / page_size)])
-    are copied into a compact local pool -- in a random order when
-    ``shuffle_seed`` is given, so the local pool is a permuted layout like the
-    global one -- and the block table is rewritten to local page ids. Unused
-    trailing block-table entries become 0. Works for numpy or torch inputs.
+    The distinct pages its sequences reference (block_table[b, :ceil(seq_b /
+    page_size)]) are gathered, on the device the global caches live on, into
+    a compact local pool -- in ascending global page order, or in a random
+    order when ``shuffle_seed`` is given so that the local pool is a permuted
+    layout like the global one -- and the block table is rewritten to local
+    page ids by one ``torch.unique(..., return_inverse=True)``. Unused
+    trailing block-table entries become 0. Only the shard moves to ``device``.
+    Works for numpy or torch inputs.
     """
-    t = lambda a: a if isinstance(a, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(a))  # noqa: E731
-    q, k_cache, v_cache, block_table, seq_lens = map(t, (q, k_cache, v_cache, block_table, seq_lens))
+    q, k_cache, v_cache, block_table, seq_lens = map(_as_tensor, (q, k_cache, v_cache, block_table, seq_lens))
     lo, hi = shard_range(q.shape[0], world, rank)
     page_size = k_cache.shape[1]
-    sl = seq_lens[lo:hi].to(torch.int64).clamp(min=0)
-    bt = block_table[lo:hi].to(torch.int64)
+    src = k_cache.device
+    sl = seq_lens[lo:hi].to(device=src, dtype=torch.int64).clamp(min=0)
     need = (sl + page_size - 1) // page_size
-    width = max(int(need.max().item()) if len(need) else 0, 1)
-    used = [bt[i, : int(need[i])] for i in range(hi - lo)]
-    glob = torch.cat(used) if used else torch.zeros(0, dtype=torch.int64)
-    # distinct pages in first-use order (a page shared by sequences is copied once)
-    uniq, first = np.unique(glob.cpu().numpy(), return_index=True)
-    order = uniq[np.argsort(first)]
-    if shuffle_seed is not None and len(order):
-        order = order[np.random.default_rng(shuffle_seed).permutation(len(order))]
-    page_map = torch.from_numpy(order.astype(np.int64))
-    lookup = {int(g): i for i, g in enumerate(order)}
-    local_bt = torch.zeros((hi - lo, width), dtype=torch.int32)
-    for i, row in enumerate(used):
-        if len(row):
-            local_bt[i, : len(row)] = torch.tensor([lookup[int(g)] for g in row], dtype=torch.int32)
-    idx = page_map.to(k_cache.device)
-    if len(page_map):
-        k_loc, v_loc = k_cache.index_select(0, idx), v_cache.index_select(0, idx)
+    width = max(int(need.max().item()) if need.numel() else 0, 1)
+    bt = block_table[lo:hi, :width].to(device=src, dtype=torch.int64)
+    if bt.shape[1] < width:
+        raise ValueError("seq_lens address more pages than block_table holds")
+    mask = torch.arange(width, device=src)[None, :] < need[:, None]
+    glob = bt[mask]
+    uniq, inv = torch.unique(glob, return_inverse=True)
+    if shuffle_seed is not None and uniq.numel():
+        gen = torch.Generator().manual_seed(shuffle_seed)
+        perm = torch.randperm(uniq.numel(), generator=gen).to(src)  # local page i holds uniq[perm[i]]
+        where = torch.empty_like(perm)
+        where[perm] = torch.arange(perm.numel(), device=src)
+        page_map, local_ids = uniq[perm], where[inv]
     else:
-        k_loc = k_cache[:1].clone()
-        v_loc = v_cache[:1].clone()
-    dev = device if device is not None else k_cache.device
+        page_map, local_ids = uniq, inv
+    local_bt = torch.zeros((hi - lo, width), dtype=torch.int32, device=src)
+    local_bt[mask] = local_ids.to(torch.int32)
+    if page_map.numel():
+        k_loc, v_loc = k_cache.index_select(0, page_map), v_cache.index_select(0, page_map)
+    else:  # an all-empty shard still gets a one-page pool (never read)
+        k_loc, v_loc = k_cache[:1].clone(), v_cache[:1].clone()
+    dev = device if device is not None else src
     return LocalShard(lo, hi, q[lo:hi].to(dev), k_loc.to(dev), v_loc.to(dev), local_bt.to(dev),
-                      seq_lens[lo:hi].to(torch.int32).to(dev), page_map)
+                      seq_lens[lo:hi].to(torch.int32).to(dev), page_map.cpu())
 
 
 def gather_to_rank0(out_local: torch.Tensor, batch: int, world: int, group=None):
@@ -91,8 +114,11 @@ def gather_to_rank0(out_local: torch.Tensor, batch: int, world: int, group=None)
     rank = dist.get_rank(group)
     sizes = [shard_range(batch, world, r) for r in range(world)]
     rows = max(h - l for l, h in sizes)
-    pad = torch.zeros((rows,) + tuple(out_local.shape[1:]), dtype=out_local.dtype, device=out_local.device)
-    pad[: out_local.shape[0]] = out_local
+    if out_local.shape[0] == rows:
+        pad = out_local.contiguous()
+    else:
+        pad = torch.zeros((rows,) + tuple(out_local.shape[1:]), dtype=out_local.dtype, device=out_local.device)
+        pad[: out_local.shape[0]] = out_local
     bucket = [torch.empty_like(pad) for _ in range(world)] if rank == 0 else None
     dist.gather(pad, bucket, dst=0, group=group)
     if rank != 0:
@@ -100,15 +126,46 @@ def gather_to_rank0(out_local: torch.Tensor, batch: int, world: int, group=None)
     return torch.cat([bucket[r][: h - l] for r, (l, h) in enumerate(sizes)], dim=0)
 
 
+class ShardedDecoder:
+    """The batch-sharded launcher of one rank.
+
+    ``decode(shard)`` runs the single-GPU B200 decode on this rank's local
+    shard, on the current stream of ``device`` -- the same call on every rank,
+    with no collective and no host synchronisation -- into a reused output
+    buffer. ``gather()`` collects the last outputs on rank 0 in global
+    sequence order (one NCCL gather; call it only when rank 0 needs them)."""
+
+    def __init__(self, batch_total: int, world: int, rank: int, device, group=None):
+        self.batch_total, self.world, self.rank = batch_total, world, rank
+        self.device = torch.device(device)
+        self.group = group
+        self.lo, self.hi = shard_range(batch_total, world, rank)
+        self._out: torch.Tensor | None = None
+
+    def decode(self, shard: LocalShard, num_splits=None, scale=None) -> torch.Tensor:
+        from .kernel_cuda_v4 import paged_attention_decode_cuda_v4
+
+        if (shard.lo, shard.hi) != (self.lo, self.hi):
+            raise ValueError(f"rank {self.rank} owns sequences [{self.lo}, {self.hi}), "
+                             f"the shard holds [{shard.lo}, {shard.hi})")
+        if self._out is None or self._out.shape != shard.q.shape:
+            self._out = torch.empty(shard.q.shape, dtype=torch.float16, device=self.device)
+        return paged_attention_decode_cuda_v4(shard.q, shard.k_cache, shard.v_cache, shard.block_table,
+                                              shard.seq_lens, num_splits=num_splits, scale=scale, out=self._out)
+
+    def gather(self, out_local: torch.Tensor | None = None):
+        out = self._out if out_local is None else out_local
+        return gather_to_rank0(out, self.batch_total, self.world, self.group)
+
+
 def decode_sharded(q, k_cache, v_cache, block_table, seq_lens, *, world: int, rank: int, device,
                    num_splits=None, scale=None, gather: bool = True, shuffle_seed: int | None = None):
-    """Localize this rank's shard, decode it on `device` and (optionally)
-    gather the outputs to rank 0. Returns (local output, gathered or None)."""
-    from .kernel_cuda_v4 import paged_attention_decode_cuda_v4
-
+    """Localize this rank's shard of a global problem (only its pages go to
+    `device`), decode it and (optionally) gather the outputs to rank 0.
+    Returns (local output, gathered or None)."""
     shard = localize(q, k_cache, v_cache, block_table, seq_lens, world, rank, device=device,
                      shuffle_seed=shuffle_seed)
-    out = paged_attention_decode_cuda_v4(shard.q, shard.k_cache, shard.v_cache, shard.block_table,
-                                         shard.seq_lens, num_splits=num_splits, scale=scale)
-    full = gather_to_rank0(out, q.shape[0], world) if gather else None
+    dec = ShardedDecoder(q.shape[0], world, rank, device)
+    out = dec.decode(shard, num_splits=num_splits, scale=scale)
+    full = dec.gather(out) if gather else None
     return out, full

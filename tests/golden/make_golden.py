@@ -4,11 +4,11 @@ Runs the reference project's own fp32 oracle ``paged_attention_decode_reference`
 (src/reference.py:8-54, imported from the reference checkout) and its
 independent SDPA oracle (tests/oracle_sdpa.py:17-58) on every case of
 ``golden_cases.py`` and stores, per case, the outputs and a digest of the
-inputs. Needs the reference checkout (default ``/root/reference``, or the
-``PAD_REFERENCE_ROOT`` environment variable); the tests only read the
-resulting .npz.
+inputs. Needs a checkout of the reference project, given as the first
+argument or in the ``PAD_REFERENCE_ROOT`` environment variable; the tests
+only read the resulting .npz.
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <path to the reference checkout>
 """
 
 from __future__ import annotations
@@ -29,7 +29,10 @@ from golden_cases import golden_cases, input_digest  # noqa: E402
 
 
 def main() -> None:
-    ref_root = os.environ.get("PAD_REFERENCE_ROOT", "/root/reference")
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("PAD_REFERENCE_ROOT")
+    if not ref_root or not os.path.isfile(os.path.join(ref_root, "src", "reference.py")):
+        raise SystemExit("usage: make_golden.py <reference checkout> (or set PAD_REFERENCE_ROOT); "
+                         "it must contain src/reference.py")
     sys.path.insert(0, ref_root)
     from src.reference import paged_attention_decode_reference  # the reference's oracle
     from tests.oracle_sdpa import sdpa_oracle  # the reference's independent oracle

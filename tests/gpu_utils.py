@@ -3,8 +3,10 @@
 Tolerance (on fp16 outputs vs the fp32 reference oracle
 run on the same fp16-rounded inputs): elementwise
     |out - ref| <= ATOL + RTOL * |ref|,  ATOL = 2e-3, RTOL = 1e-2,
-plus max |out - ref| <= ATOL over all elements. Max-rel is reported over
-elements with |ref| >= 1e-2 (relative error is meaningless near zero).
+plus max |out - ref| <= ATOL over all elements, plus max-rel
+max(|out - ref| / |ref|) <= RTOL over the elements with |ref| >= REL_FLOOR
+(1e-2; relative error is meaningless near zero, where the absolute bound
+governs). All three are asserted.
 """
 
 from __future__ import annotations
@@ -15,6 +17,7 @@ import torch
 import pad_b200
 
 ATOL, RTOL = 2e-3, 1e-2
+REL_FLOOR = 1e-2
 
 
 def to_gpu(case, device="cuda"):
@@ -36,9 +39,10 @@ def assert_parity(actual, expected, what=""):
     err = np.abs(actual - expected)
     bound = ATOL + RTOL * np.abs(expected)
     bad = err > bound
-    big = np.abs(expected) >= 1e-2
+    big = np.abs(expected) >= REL_FLOOR
     rel = float((err[big] / np.abs(expected[big])).max()) if big.any() else 0.0
     assert not bad.any(), (f"{what}: {int(bad.sum())} elements out of tolerance; max abs {err.max():.3e}, "
                            f"max rel {rel:.3e}")
     assert err.max() <= ATOL, f"{what}: max abs error {err.max():.3e} > {ATOL}"
+    assert rel <= RTOL, f"{what}: max rel error {rel:.3e} > {RTOL} (over |ref| >= {REL_FLOOR})"
     return float(err.max()), rel

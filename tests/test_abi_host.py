@@ -54,10 +54,10 @@ def _decode(**over):
 def test_abi_rejects_bad_shapes_without_touching_a_device():
     assert _decode(batch=-1) == _lib.PAD_ERR_INVALID_ARGUMENT
     assert _decode(hq=10, hkv=4) == _lib.PAD_ERR_INVALID_ARGUMENT
+    assert b"divisible" in _lib.load().pad_last_error()
     assert _decode(ps=0) == _lib.PAD_ERR_INVALID_ARGUMENT
     assert _decode(qs=None) == _lib.PAD_ERR_INVALID_ARGUMENT
     assert _decode(scale=float("nan")) == _lib.PAD_ERR_INVALID_ARGUMENT
-    assert b"divisible" in _lib.load().pad_last_error() or True
     # batch 0 is a no-op
     assert _decode(batch=0) == _lib.PAD_OK
     # null tensors
@@ -72,6 +72,35 @@ def test_abi_rejects_bad_shapes_without_touching_a_device():
     assert _decode(**base, bts=2) == _lib.PAD_ERR_INVALID_ARGUMENT
 
 
+def _append(**over):
+    lib = _lib.load()
+    kw = dict(kn=0, vn=0, k=0, v=0, bt=0, pos=0, batch=2, hkv=2, d=128, pages=10, ps=16, maxp=4,
+              kns=[256, 128, 1], vns=[256, 128, 1], ks=[4096, 256, 128, 1], vs=[4096, 256, 128, 1], bts=4)
+    kw.update(over)
+    arr = lambda x: None if x is None else _lib.i64_array(x)  # noqa: E731
+    return lib.pad_paged_kv_append(kw["kn"], kw["vn"], kw["k"], kw["v"], kw["bt"], kw["pos"], kw["batch"], kw["hkv"],
+                                   kw["d"], kw["pages"], kw["ps"], kw["maxp"], arr(kw["kns"]), arr(kw["vns"]),
+                                   arr(kw["ks"]), arr(kw["vs"]), kw["bts"], 0, 0)
+
+
+def test_kv_append_errors_set_the_last_error_text():
+    """Every non-OK status of pad_paged_kv_append comes with its own message
+    (never a stale one from an earlier call)."""
+    lib = _lib.load()
+    assert _decode(hq=10, hkv=4) == _lib.PAD_ERR_INVALID_ARGUMENT  # leaves a decode message behind
+    assert _append(batch=-1) == _lib.PAD_ERR_INVALID_ARGUMENT
+    assert b"kv_append" in lib.pad_last_error() and b"size" in lib.pad_last_error()
+    assert _append() == _lib.PAD_ERR_INVALID_ARGUMENT
+    assert b"null" in lib.pad_last_error()
+    p = 1 << 20
+    base = dict(kn=p, vn=p, k=p, v=p, bt=p, pos=p)
+    assert _append(**base, bts=2) == _lib.PAD_ERR_INVALID_ARGUMENT
+    assert b"stride" in lib.pad_last_error()
+    assert _append(**base, ks=[4096, 256, 128, 2]) == _lib.PAD_ERR_UNSUPPORTED
+    assert b"contiguous" in lib.pad_last_error()
+    assert _append(batch=0) == _lib.PAD_OK
+
+
 def test_wrapper_contract_asserts_on_cpu_tensors():
     q = torch.zeros(1, 12, 128, dtype=torch.float16)
     k = torch.zeros(4, 16, 2, 128, dtype=torch.float16)
@@ -79,6 +108,8 @@ def test_wrapper_contract_asserts_on_cpu_tensors():
     sl = torch.ones(1, dtype=torch.int32)
     with pytest.raises(AssertionError):
         pad_b200.paged_attention_decode_cuda_v4(q, k, k, bt, sl)
+    with pytest.raises(AssertionError):  # the Triton-v4 twin asserts the same contract
+        pad_b200.paged_attention_decode_v4(q, k, k, bt, sl)
 
 
 @pytest.mark.parametrize("seed", range(12))

@@ -4,6 +4,7 @@ split invariance, oversplit, page boundary, GQA ratios, ragged batches, fuzz;
 plus the golden fixtures, every BASELINE config, and size-independent
 properties at full size."""
 
+import functools
 import os
 
 import numpy as np
@@ -48,12 +49,23 @@ def test_split_invariance_seq_2000(num_splits):
     assert_parity(run(c, num_splits=num_splits), ref, f"S={num_splits}")
 
 
-@pytest.mark.parametrize("seq_len", [8192, 32768])
-@pytest.mark.parametrize("num_splits", [1, 2, 4, 8, 16, 32, 64, None])
-def test_split_invariance_long_context_c3(seq_len, num_splits):
-    c = config_case("c3", batch=1, seq_len=seq_len, seed=seq_len)
-    ref = oracle.decode_c(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens)
-    assert_parity(run(c, num_splits=num_splits), ref, f"seq={seq_len} S={num_splits}")
+@functools.lru_cache(maxsize=8)
+def _c3_case(batch, seq_len):
+    c = config_case("c3", batch=batch, seq_len=seq_len, seed=seq_len + batch)
+    return c, oracle.decode_c(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens)
+
+
+C3_SPLITS = [1, 2, 4, 8, 16, 32, 64, None]
+
+
+@pytest.mark.parametrize("batch,seq_len", [(1, 8192), (1, 32768), (4, 8192), (4, 32768), (1, 131072)])
+@pytest.mark.parametrize("num_splits", C3_SPLITS)
+def test_split_invariance_long_context_c3(batch, seq_len, num_splits):
+    """page 32, N(0, 0.5) inputs, batch 1 and 4, every
+    num_splits of the sweep (tests/test_kernel_cuda_v4.py:62-76 of the
+    reference checks split invariance the same way)."""
+    c, ref = _c3_case(batch, seq_len)
+    assert_parity(run(c, num_splits=num_splits), ref, f"B={batch} seq={seq_len} S={num_splits}")
 
 
 def test_c3_131072_batch4():
@@ -250,3 +262,18 @@ def test_reused_workspace_split_then_empty_pair():
     assert np.all(out[0] == 0)
     ref = oracle.decode_c(b.q, b.k_cache, b.v_cache, b.block_table, b.seq_lens)
     assert_parity(out, ref)
+
+
+@pytest.mark.parametrize("block_n", [16, 64, 128, 256])
+def test_triton_twin_signature(block_n):
+    """The reference's Triton-v4 call surface (src/kernel_v4_split_k.py:213-222):
+    num_splits defaults to 16, block_n is validated like the reference's and
+    otherwise only accepted -- the B200 kernel picks its own token tile."""
+    c = explicit_case([1, 300, 2500], num_kv_heads=2, gqa_ratio=6, head_dim=128, page_size=16, seed=77)
+    ref = oracle.decode_c(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens)
+    q, k, v, bt, sl = to_gpu(c)
+    out = pad_b200.paged_attention_decode_v4(q, k, v, bt, sl, block_n=block_n)
+    assert_parity(out.float().cpu().numpy(), ref, f"block_n={block_n}")
+    out = pad_b200.paged_attention_decode_v4(q, k, v, bt, sl, num_splits=3, scale=0.05, block_n=block_n)
+    ref2 = oracle.decode_c(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens, scale=0.05)
+    assert_parity(out.float().cpu().numpy(), ref2, f"block_n={block_n} S=3 scale=0.05")

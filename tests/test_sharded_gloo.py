@@ -74,3 +74,36 @@ def test_gloo_gather_to_rank0_in_sequence_order(world):
     q = ctx.Queue()
     mp.start_processes(_worker, args=(world, _free_port(), q), nprocs=world, join=True, start_method="spawn")
     assert q.get(timeout=60) == 0.0
+
+
+def test_local_pool_holds_only_the_shards_pages():
+    """A rank's pool holds exactly the distinct pages its own sequences use
+    (a page shared by two sequences is copied once), and the remapped block
+    table addresses the same rows as the global one."""
+    c = explicit_case([40, 0, 333, 17, 128, 600, 5], num_kv_heads=2, gqa_ratio=4, head_dim=32, page_size=8, seed=3)
+    bt = c.block_table.copy()
+    bt[1, 0] = bt[0, 0]  # sequence 1 is empty: its entries are never used
+    bt[3, 1] = bt[2, 3]  # sequences 2 and 3 share a page
+    for world in (1, 2, 4):
+        for rank in range(world):
+            sh = localize(c.q, c.k_cache, c.v_cache, bt, c.seq_lens, world, rank, shuffle_seed=rank)
+            used = set()
+            for b in range(sh.lo, sh.hi):
+                used |= set(bt[b, : (int(c.seq_lens[b]) + 7) // 8].tolist())
+            assert sh.k_cache.shape[0] == max(len(used), 1)
+            assert set(sh.page_map.tolist()) == used
+            for i, b in enumerate(range(sh.lo, sh.hi)):
+                n = (int(c.seq_lens[b]) + 7) // 8
+                glob = bt[b, :n]
+                loc = sh.block_table[i, :n].numpy()
+                assert np.array_equal(sh.page_map.numpy()[loc], glob)
+                np.testing.assert_array_equal(sh.k_cache.numpy()[loc], c.k_cache[glob])
+
+
+def test_sharded_decoder_rejects_another_ranks_shard():
+    from pad_b200.sharded import ShardedDecoder
+
+    c = explicit_case([40, 7, 333], num_kv_heads=2, gqa_ratio=4, head_dim=32, page_size=8, seed=3)
+    sh = localize(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens, 2, 1)
+    with pytest.raises(ValueError, match="owns sequences"):
+        ShardedDecoder(3, 2, 0, "cpu").decode(sh)

@@ -77,3 +77,35 @@ def test_sharded_decode_matches_oracle():
     mp.start_processes(_worker, args=(world, _port(), qq), nprocs=world, join=True, start_method="spawn")
     ok, max_err = qq.get(timeout=60)
     assert ok and max_err <= 2e-3, f"world={world}: max abs err {max_err:.3e}"
+
+
+@pytest.mark.timeout(600)
+def test_c5_shape_shard_built_with_localize():
+    """BASELINE config 5 at its own shape on one GPU: Llama-3-70B heads
+    (64 Q / 8 KV, head_dim 128, page 16), seq_lens U{1024..16384} with seed 2.
+    A 256-sequence global problem (its first 256 lengths) lives on the GPU;
+    rank 1 of 2 takes its 128 sequences with ``localize`` (only its pages are
+    copied, into a permuted local pool) and decodes them through the
+    launcher. 32 sampled sequences plus the longest and shortest are checked
+    against the CPU oracle."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from pad_b200.cases import config_case, config_seq_lens
+    from pad_b200.sharded import ShardedDecoder, localize
+
+    sl = config_seq_lens("c5")[:256]
+    g = config_case("c5", seq_lens=sl, device="cuda", seed=5)
+    sh = localize(g.q, g.k_cache, g.v_cache, g.block_table, g.seq_lens, 2, 1, shuffle_seed=1)
+    assert sh.k_cache.shape[0] == int(((sl[128:] + 15) // 16).sum())
+    del g
+    torch.cuda.empty_cache()
+    dec = ShardedDecoder(256, 2, 1, "cuda")
+    out = dec.decode(sh).float().cpu().numpy()
+    lens = sh.seq_lens.cpu().numpy()
+    idx = np.random.default_rng(0).choice(len(lens), 32, replace=False)
+    idx = np.unique(np.concatenate([idx, [int(np.argmax(lens)), int(np.argmin(lens))]]))
+    ti = torch.from_numpy(idx).cuda()
+    sub = localize(sh.q[ti], sh.k_cache, sh.v_cache, sh.block_table[ti], sh.seq_lens[ti], 1, 0, device="cpu")
+    ref = oracle.decode_c(sub.q.numpy(), sub.k_cache.numpy(), sub.v_cache.numpy(), sub.block_table.numpy(),
+                          sub.seq_lens.numpy())
+    assert_parity(out[idx], ref, "C5 shard (sampled)")
