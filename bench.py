@@ -11,19 +11,40 @@ on. A step is one decode call over the whole batch. ``value`` is achieved
 KV-read bandwidth in TB/s: algorithmic bytes (sum_b seq_b * Hkv * D * 2 (K,V)
 * 2 B, the reference's bench/roofline.py:55-59 formula) / device time, summed
 over ranks (each rank decodes its own batch: weak scaling, no collective).
-Extra keys give the full batch sweep and the long-context point (config 3,
-batch 1, seq 32768).
+
+Extra keys (all printed by this script; the design notes cite them by name):
+  sweep_c2_seq4096        C2 batch 1..64
+  c2_b64_wide_table       C2 batch 64 with a block table twice as wide as the
+                          sequences need (a serving engine's table)
+  long_context_c3_batch1  C3 batch 1 at seq 8k / 32k / 128k (heuristic splits)
+  num_splits_sweep_c3     C3 seq 32k, batch 1 and 4, num_splits 1..64 and the
+                          heuristic (bench/bench_cuda_v4_num_splits.py:78-149
+                          of the reference sweeps the same way)
+  c4_llama8b_b256         C4, the ragged Llama-3-8B batch of 256
+  c5_strong               C5 (1024 Llama-3-70B sequences) split over the N
+                          ranks through pad_b200.sharded.ShardedDecoder: strong
+                          scaling, max-rank device time, gather time, sampled
+                          oracle check
+  host_us_per_call        CPU time of one paged_attention_decode_cuda_v4 call
+                          (resident inputs, no copies, no sync inside)
+  e2e / e2e_kv_resident   through the public API with host buffers
+  cpu_baseline / cpu_port the reference's CPU path (src/reference.py as
+                          shipped) / the C restatement, on the host cores
+  same_box_*              the reference's Triton v4 and FlashInfer, timed the
+                          same way (comparators, never on our path)
 
 Timing: inputs are rotated over independent KV pools whose total exceeds L2
 (126 MB), so every step reads HBM; steps are recorded once into a CUDA graph
-(the per-call host overhead is measured separately in ``e2e``) and replayed;
-CUDA events on the launching stream bracket exactly K steps, with a barrier
-and device synchronisation on both sides; multi-GPU takes the max over ranks.
+(the per-call host overhead is measured separately) and replayed; CUDA events
+on the launching stream bracket exactly K steps, with a barrier and device
+synchronisation on both sides; multi-GPU takes the max over ranks.
 ``nvidia-smi`` samples clocks during the timed region.
 
-``--impl reference`` times the reference algorithm's CPU implementation -- the
-C restatement of src/reference.py in oracle/ (the reference is Python and
-cannot be compiled) -- on the host cores for the same workload and metric.
+``--impl reference`` times the reference's own CPU implementation of the
+path -- ``paged_attention_decode_reference`` of src/reference.py, imported
+unmodified from the offline install in baseline/_ref, on fp32 CPU tensors
+with all host threads -- on a bounded sample of the same workload. Without
+that install it falls back to the C restatement in oracle/ (kind "port").
 """
 
 from __future__ import annotations
@@ -42,11 +63,13 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 for _p in (REPO, os.path.join(REPO, "paged-attention-decode_b200")):
     if _p not in sys.path:
         sys.path.insert(0, _p)
+REF_DIR = os.path.join(REPO, "baseline", "_ref")
 
 import numpy as np  # noqa: E402
 
 L2_BYTES = 126 * 2**20
 GRAPH_STEPS = 100  # steps recorded per CUDA graph; the graph is replayed to reach K
+C5_BATCH = 1024
 
 
 def parse():
@@ -56,15 +79,16 @@ def parse():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="c2", choices=["c2", "c3", "c4", "c5"])
-    ap.add_argument("--no-sweep", action="store_true", help="skip the batch sweep / long-context extras")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the sweeps and the same-box comparators")
     ap.add_argument("--no-extras", action="store_true",
-                    help="time the workload only (no e2e, CPU baseline or sweep); used for ncu captures")
+                    help="time the workload only (no e2e, CPU baseline, C5 or sweeps); used for ncu captures")
     return ap.parse_args()
 
 
 def workload_spec(name: str, n_gpus: int, rank: int):
     """(config name, batch, seq_len, seq_lens override) for this rank."""
     from pad_b200.cases import config_seq_lens
+    from pad_b200.sharded import shard_range
 
     if name == "c2":
         return "c2", 64, 4096, None
@@ -73,10 +97,29 @@ def workload_spec(name: str, n_gpus: int, rank: int):
     if name == "c4":
         return "c4", 256, None, None
     if name == "c5":  # batch 1024 split evenly by sequence across the GPUs
-        sl = config_seq_lens("c5")
-        per = len(sl) // n_gpus
-        return "c5", per, None, sl[rank * per:(rank + 1) * per]
+        lo, hi = shard_range(C5_BATCH, n_gpus, rank)
+        return "c5", hi - lo, None, config_seq_lens("c5")[lo:hi]
     raise KeyError(name)
+
+
+def metric_name(workload: str) -> str:
+    if workload == "c2":
+        return "decode-attn achieved KV HBM TB/s (Qwen2.5-1.5B shape, seq 4096, batch 64)"
+    return f"decode-attn achieved KV HBM TB/s ({workload})"
+
+
+def workload_config(workload: str, world: int) -> dict:
+    """The `config` object, identical in both arms for the same workload."""
+    from pad_b200.cases import CONFIGS
+
+    cfg, batch, seq_len, _ = workload_spec(workload, world, 0)
+    hq, hkv, d, ps, std = CONFIGS[cfg]
+    wl = {"c2": "c2 batch=64 per GPU seq=4096", "c3": "c3 batch=1 per GPU seq=32768",
+          "c4": "c4 batch=256 per GPU, ragged", "c5": f"c5 batch={C5_BATCH} split over {world} GPUs"}[workload]
+    return {"workload": wl, "heads_q_kv": [hq, hkv], "head_dim": d, "page_size": ps,
+            "inputs": f"fp16 N(0,{std}) q/K/V, random page permutation",
+            "l2": "GPU arm: inputs rotated over independent KV pools totalling > 2.5x L2; CPU arm: host memory",
+            "parallelism": f"batch-sharded x{world}, no collective on the decode path"}
 
 
 def peaks():
@@ -89,12 +132,18 @@ def peaks():
 
 
 def committed_traffic():
-    """dram bytes per launch of the decode kernel from the committed ncu summary."""
+    """DRAM bytes per launch of the decode kernel at C2 batch 64, from the
+    committed ncu summary (measured once with ncu, not in this run)."""
     path = os.path.join(REPO, "profiles", "decode_stream_kernel_c2_b64.md")
     if not os.path.exists(path):
         return None
     m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", open(path).read())
     return float(m.group(1)) if m else None
+
+
+def rate(nbytes, ms, peak_gbs):
+    return {"us_per_call": round(ms * 1e3, 3), "TB_s": round(nbytes / (ms * 1e-3) / 1e12, 4),
+            "frac_of_measured_hbm": round(nbytes / (ms * 1e-3) / 1e9 / peak_gbs, 4)}
 
 
 # ------------------------------------------------------------------ clocks
@@ -145,21 +194,22 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ our arm
-def make_pools(cfg, batch, seq_len, seq_lens, device, min_bytes):
+def make_pools(cfg, batch, seq_len, seq_lens, device, min_bytes, table_width=None):
     from pad_b200.cases import config_case, kv_bytes
 
-    first = config_case(cfg, batch=batch, seq_len=seq_len, seq_lens=seq_lens, device=device, seed=0)
+    kw = dict(batch=batch, seq_len=seq_len, seq_lens=seq_lens, device=device, table_width=table_width)
+    first = config_case(cfg, seed=0, **kw)
     per = kv_bytes(first.seq_lens.cpu().numpy(), first.k_cache.shape[2], first.k_cache.shape[3])
     # one pool is enough once a single step streams well past L2 (C5: ~36 GB)
     n = 1 if per >= min_bytes else max(2, min(64, math.ceil(min_bytes / max(per, 1))))
-    pools = [first] + [config_case(cfg, batch=batch, seq_len=seq_len, seq_lens=seq_lens, device=device, seed=i)
-                       for i in range(1, n)]
+    pools = [first] + [config_case(cfg, seed=i, **kw) for i in range(1, n)]
     return pools, per
 
 
-def time_device(pools, steps, warmup, torch, barrier, fn=None):
+def time_device(pools, steps, warmup, torch, barrier, fn=None, num_splits=None):
     """Device time of `steps` decode calls rotated over `pools` (ms). `fn(case)`
-    replaces the call of this package (used for the same-box comparator)."""
+    replaces the call of this package (used for the launcher and the
+    same-box comparators)."""
     import pad_b200
 
     stream = torch.cuda.Stream()
@@ -171,7 +221,7 @@ def time_device(pools, steps, warmup, torch, barrier, fn=None):
             fn(c)
             return
         pad_b200.paged_attention_decode_cuda_v4(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens,
-                                                out=outs[i % len(pools)])
+                                                num_splits=num_splits, out=outs[i % len(pools)])
 
     with torch.cuda.stream(stream):
         for i in range(max(warmup, len(pools))):
@@ -207,7 +257,7 @@ def time_device(pools, steps, warmup, torch, barrier, fn=None):
     return start.elapsed_time(end)
 
 
-def time_e2e(pool, steps, torch):
+def time_e2e(pool, steps, torch, barrier):
     """Through the public API with host buffers: per step H2D of every input
     (q, k_cache, v_cache, block_table, seq_lens) from pinned memory, the
     decode, and D2H of the output. Returns (ms per step, h2d bytes, d2h bytes)."""
@@ -229,11 +279,13 @@ def time_e2e(pool, steps, torch):
         step()
     torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
     s.record()
     for _ in range(steps):
         step()
     e.record()
     torch.cuda.synchronize()
+    barrier()
     return s.elapsed_time(e) / steps, h2d, d2h
 
 
@@ -246,12 +298,13 @@ def time_e2e_resident(pool, steps, torch):
     host = [t.cpu().pin_memory() for t in (pool.q, pool.block_table, pool.seq_lens)]
     dev = [torch.empty_like(t, device="cuda") for t in host]
     out_h = torch.empty(pool.q.shape, dtype=torch.float16).pin_memory()
+    out_d = torch.empty_like(pool.q)
 
     def step():
         for d, h in zip(dev, host):
             d.copy_(h, non_blocking=True)
-        o = pad_b200.paged_attention_decode_cuda_v4(dev[0], pool.k_cache, pool.v_cache, dev[1], dev[2])
-        out_h.copy_(o, non_blocking=True)
+        pad_b200.paged_attention_decode_cuda_v4(dev[0], pool.k_cache, pool.v_cache, dev[1], dev[2], out=out_d)
+        out_h.copy_(out_d, non_blocking=True)
 
     for _ in range(5):
         step()
@@ -266,6 +319,27 @@ def time_e2e_resident(pool, steps, torch):
         out_h.numel() * out_h.element_size()
 
 
+def host_us_per_call(pool, torch, calls=200):
+    """CPU wall time of one paged_attention_decode_cuda_v4 call on resident
+    inputs (no copies, no synchronisation inside the loop; the launches only
+    queue, so this is the host cost of the wrapper and the C-ABI call)."""
+    import pad_b200
+
+    out = torch.empty_like(pool.q)
+    args = (pool.q, pool.k_cache, pool.v_cache, pool.block_table, pool.seq_lens)
+    for _ in range(10):
+        pad_b200.paged_attention_decode_cuda_v4(*args, out=out)
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(5):
+        t0 = time.perf_counter()
+        for _ in range(calls):
+            pad_b200.paged_attention_decode_cuda_v4(*args, out=out)
+        best = min(best, (time.perf_counter() - t0) / calls * 1e6)
+        torch.cuda.synchronize()
+    return round(best, 2)
+
+
 def reference_gpu_comparator(torch, barrier, peak_gbs):
     """The reference's own GPU kernel timed on this box the same way (CUDA-graph
     replay over KV pools rotated past L2): its Triton v4 split-K kernel
@@ -273,16 +347,15 @@ def reference_gpu_comparator(torch, barrier, peak_gbs):
     install of the reference in baseline/_ref. Recorded beside our numbers,
     not a target. Its CUDA v4 kernel is not in that install (the package
     carries no .cu sources), so it cannot be built here."""
-    ref_dir = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
-    if not os.path.isfile(os.path.join(ref_dir, "kernel_v4_split_k.py")):
+    if not os.path.isfile(os.path.join(REF_DIR, "kernel_v4_split_k.py")):
         return {"unavailable": "baseline/_ref (offline install of the reference) is absent"}
-    sys.path.insert(0, ref_dir)
+    sys.path.insert(0, REF_DIR)
     try:
         import kernel_v4_split_k as ref_tv4
     except Exception as e:  # noqa: BLE001 -- report, do not fail the bench
         return {"unavailable": f"importing the reference Triton v4 failed: {e!r}"[:200]}
     finally:
-        sys.path.remove(ref_dir)
+        sys.path.remove(REF_DIR)
     import pad_b200
 
     def fn(c):
@@ -295,9 +368,7 @@ def reference_gpu_comparator(torch, barrier, peak_gbs):
         ours = pad_b200.paged_attention_decode_cuda_v4(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens)
         diff = (fn(c).float() - ours.float()).abs().max().item()
         m = time_device(pl, 200, 5, torch, barrier, fn=fn) / 200
-        res[f"{cfg}_batch{b}_seq{sl}"] = {"us_per_call": round(m * 1e3, 3), "TB_s": round(nb / (m * 1e-3) / 1e12, 4),
-                                         "frac_of_measured_hbm": round(nb / (m * 1e-3) / 1e9 / peak_gbs, 4),
-                                         "max_abs_diff_vs_ours": diff}
+        res[f"{cfg}_batch{b}_seq{sl}"] = dict(rate(nb, m, peak_gbs), max_abs_diff_vs_ours=diff)
         del pl
     return res
 
@@ -340,81 +411,158 @@ def flashinfer_comparator(torch, barrier, peak_gbs):
             ours = pad_b200.paged_attention_decode_cuda_v4(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens)
             diff = (fn(c).float() - ours.float()).abs().max().item()
             m = time_device(pl, 200, 5, torch, barrier, fn=fn) / 200
-            res[f"{cfg}_batch{b}_seq{sl}"] = {"us_per_call": round(m * 1e3, 3),
-                                             "TB_s": round(nb / (m * 1e-3) / 1e12, 4),
-                                             "frac_of_measured_hbm": round(nb / (m * 1e-3) / 1e9 / peak_gbs, 4),
-                                             "max_abs_diff_vs_ours": diff}
+            res[f"{cfg}_batch{b}_seq{sl}"] = dict(rate(nb, m, peak_gbs), max_abs_diff_vs_ours=diff)
             del pl, wraps
     except Exception as e:  # noqa: BLE001
         res["unavailable"] = f"flashinfer run failed: {e!r}"[:200]
     return res
 
 
-def cpu_baseline_sample(pool, seconds: float = 10.0):
-    """The C oracle (oracle/pa_oracle.c, the reference algorithm) on the host
-    cores, on a bounded sample of the workload's sequences; TB/s of KV read."""
-    import oracle
+# ------------------------------------------------------------------ CPU legs
+def _reference_fn():
+    """paged_attention_decode_reference of the reference's src/reference.py,
+    imported unmodified from the offline install (baseline/_ref), or None."""
+    if not os.path.isfile(os.path.join(REF_DIR, "reference.py")):
+        return None
+    sys.path.insert(0, REF_DIR)
+    try:
+        import reference
+    except Exception:  # noqa: BLE001 -- the caller falls back to the port
+        return None
+    finally:
+        sys.path.remove(REF_DIR)
+    return reference.paged_attention_decode_reference
 
-    q = pool.q.cpu().numpy()
-    k = pool.k_cache.cpu().numpy()
-    v = pool.v_cache.cpu().numpy()
-    bt = pool.block_table.cpu().numpy()
-    sl = pool.seq_lens.cpu().numpy()
-    threads = oracle.max_threads()
-    n = len(sl)
-    take = n
-    # size the sample so one call takes well under `seconds`
-    probe = min(n, 2)
+
+def cpu_sample(cfg, batch, seq_len, seq_lens, seconds: float, port: bool = False, steps_cap: int = 50,
+               warmup: int = 1):
+    """Time the reference's CPU path on a bounded sample of the workload: the
+    first `take` sequences of the config, sized so one step takes about
+    seconds / 4. Returns (TB/s of KV read, description, steps, step ms, kind, threads)."""
+    import torch
+
+    from pad_b200.cases import config_case, config_seq_lens, kv_bytes
+
+    sl_all = np.asarray(seq_lens if seq_lens is not None else config_seq_lens(cfg, batch, seq_len))
+    ref = None if port else _reference_fn()
+    threads = os.cpu_count() or 1
+    if ref is not None:
+        torch.set_num_threads(threads)
+        kind, what = "reference", "src/reference.py paged_attention_decode_reference (unmodified, baseline/_ref)"
+
+        def run(c):
+            t = [torch.from_numpy(np.ascontiguousarray(a)) for a in (c.q, c.k_cache, c.v_cache, c.block_table,
+                                                                     c.seq_lens)]
+            ref(*t)
+    else:
+        import oracle
+
+        threads = oracle.max_threads()
+        kind, what = "port", "C restatement of src/reference.py (oracle/pa_oracle.c)"
+
+        def run(c):
+            oracle.decode_c(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens, nthreads=threads)
+
+    # size the sample from a one-sequence probe; at most 64 sequences are built
+    probe = config_case(cfg, seq_lens=sl_all[:1])
+    run(probe)
     t0 = time.perf_counter()
-    oracle.decode_c(q[:probe], k, v, bt[:probe], sl[:probe], nthreads=threads)
+    run(probe)
     dt = max(time.perf_counter() - t0, 1e-4)
-    take = max(1, min(n, int(probe * (seconds / 4) / dt)))
-    calls, elapsed = 0, 0.0
-    t0 = time.perf_counter()
-    while elapsed < seconds and calls < 50:
-        oracle.decode_c(q[:take], k, v, bt[:take], sl[:take], nthreads=threads)
+    take = max(1, min(len(sl_all), 64, int((seconds / 4) / dt)))
+    c = config_case(cfg, seq_lens=sl_all[:take])
+    for _ in range(max(1, warmup)):
+        run(c)
+    calls, t0 = 0, time.perf_counter()
+    while calls < steps_cap and (calls < 2 or time.perf_counter() - t0 < seconds):
+        run(c)
         calls += 1
-        elapsed = time.perf_counter() - t0
-    nbytes = int(sl[:take].astype(np.int64).sum()) * k.shape[2] * k.shape[3] * 4
-    return {"value": nbytes * calls / elapsed / 1e12, "unit": "TB/s", "cores": threads, "kind": "port",
-            "sample": f"{take} of {n} sequences x {calls} calls ({elapsed:.1f} s), C oracle "
-                      f"(oracle/pa_oracle.c) on {threads} host threads"}
+    el = time.perf_counter() - t0
+    nb = kv_bytes(sl_all[:take], c.k_cache.shape[2], c.k_cache.shape[3])
+    desc = (f"{take} of {len(sl_all)} sequences per step x {calls} steps ({el:.1f} s), {what}, fp32 on "
+            f"{threads} host threads")
+    return nb * calls / el / 1e12, desc, calls, el / calls * 1e3, kind, threads
 
 
-def check_and_gather(pool, world, rank, torch):
-    """C5 bookkeeping outside the timed region: every rank checks sampled
-    sequences of its shard against the C oracle (their pages copied into a
-    compact host pool), and the outputs are gathered to rank 0 over NCCL."""
-    import oracle
-    import pad_b200
-    from pad_b200.sharded import localize
-
-    out = pad_b200.paged_attention_decode_cuda_v4(pool.q, pool.k_cache, pool.v_cache, pool.block_table,
-                                                  pool.seq_lens)
-    idx = np.random.default_rng(rank).choice(pool.q.shape[0], 4, replace=False)
-    ti = torch.from_numpy(idx).cuda()
-    sub = localize(pool.q[ti], pool.k_cache, pool.v_cache, pool.block_table[ti], pool.seq_lens[ti], 1, 0,
-                   device="cpu")
-    ref = oracle.decode_c(sub.q.numpy(), sub.k_cache.numpy(), sub.v_cache.numpy(), sub.block_table.numpy(),
-                          sub.seq_lens.numpy())
-    err = torch.tensor([float(np.abs(out[ti].float().cpu().numpy() - ref).max())], device="cuda")
-    res = {}
-    if world > 1:
-        import torch.distributed as dist
-        from pad_b200.sharded import gather_to_rank0
-
-        dist.all_reduce(err, op=dist.ReduceOp.MAX)
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        full = gather_to_rank0(out, pool.q.shape[0] * world, world)
-        torch.cuda.synchronize()
-        res["gather_to_rank0"] = {"ms": (time.perf_counter() - t0) * 1e3,
-                                  "rows": None if full is None else int(full.shape[0])}
-    res["check"] = {"sampled_sequences_per_rank": 4, "max_abs_err_vs_oracle": float(err.item()),
-                    "tolerance": "2e-3 + 1e-2*|ref|"}
+def cpu_baselines(cfg, batch, seq_len, seq_lens):
+    v, desc, _, _, kind, thr = cpu_sample(cfg, batch, seq_len, seq_lens, 10.0)
+    res = {"cpu_baseline": {"value": v, "unit": "TB/s", "cores": thr, "kind": kind, "sample": desc}}
+    if kind == "reference":
+        v2, desc2, _, _, _, thr2 = cpu_sample(cfg, batch, seq_len, seq_lens, 5.0, port=True)
+        res["cpu_port"] = {"value": v2, "unit": "TB/s", "cores": thr2, "kind": "port", "sample": desc2}
     return res
 
 
+# ------------------------------------------------------------------ C5 strong scaling
+def c5_strong(world, rank, local, torch, barrier, peak_gbs, steps=20):
+    """C5 (1024 Llama-3-70B sequences) split over the ranks: each rank builds
+    only its own sequences' KV pages, in a permuted local pool on its GPU,
+    and decodes them through the launcher (ShardedDecoder). Device time is
+    the max over ranks; the aggregate is all ranks' KV bytes over it. Then
+    the outputs are gathered to rank 0 (timed separately) and every rank
+    checks sampled sequences against the CPU oracle."""
+    import oracle
+    from pad_b200.cases import config_case, kv_bytes
+    from pad_b200.sharded import LocalShard, ShardedDecoder, localize
+
+    cfg, b, _, sl = workload_spec("c5", world, rank)
+    c = config_case(cfg, seq_lens=sl, device="cuda", seed=100 + rank)
+    dec = ShardedDecoder(C5_BATCH, world, rank, torch.device("cuda", local))
+    shard = LocalShard(dec.lo, dec.hi, c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens)
+    nb = kv_bytes(sl, c.k_cache.shape[2], c.k_cache.shape[3])
+    ms = time_device([c], steps, 3, torch, barrier, fn=lambda _c: dec.decode(shard)) / steps
+    t = torch.tensor([ms, nb, nb, nb], device="cuda", dtype=torch.float64)
+    out = dec.decode(shard)
+    # sampled oracle check of this rank's shard
+    lens = sl
+    idx = np.random.default_rng(rank).choice(len(lens), min(4, len(lens)), replace=False)
+    idx = np.unique(np.concatenate([idx, [int(np.argmax(lens))]]))
+    ti = torch.from_numpy(idx).cuda()
+    sub = localize(c.q[ti], c.k_cache, c.v_cache, c.block_table[ti], c.seq_lens[ti], 1, 0, device="cpu")
+    ref = oracle.decode_c(sub.q.numpy(), sub.k_cache.numpy(), sub.v_cache.numpy(), sub.block_table.numpy(),
+                          sub.seq_lens.numpy())
+    got = out[ti].float().cpu().numpy()
+    err = np.abs(got - ref)
+    ok = bool(np.all(err <= 2e-3 + 1e-2 * np.abs(ref)))
+    e = torch.tensor([float(err.max()), 0.0 if ok else 1.0], device="cuda", dtype=torch.float64)
+    gather_ms = None
+    if world > 1:
+        import torch.distributed as dist
+
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        mn = t.clone()
+        dist.all_reduce(mn, op=dist.ReduceOp.MIN)
+        sm = t.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        dist.all_reduce(e, op=dist.ReduceOp.MAX)
+        ms_max, bytes_total, bytes_max, bytes_min = mx[0].item(), sm[1].item(), mx[2].item(), mn[3].item()
+        ms_min = mn[0].item()
+        dec.gather(out)  # warm the collective
+        torch.cuda.synchronize()
+        barrier()
+        t0 = time.perf_counter()
+        full = dec.gather(out)
+        torch.cuda.synchronize()
+        gather_ms = (time.perf_counter() - t0) * 1e3
+        if rank == 0:
+            assert full.shape[0] == C5_BATCH
+    else:
+        ms_max = ms_min = ms
+        bytes_total = bytes_max = bytes_min = nb
+    return {"n_gpus": world, "sequences": C5_BATCH, "sequences_per_gpu_max": math.ceil(C5_BATCH / world),
+            "steps": steps,
+            "us_per_call_max_rank": round(ms_max * 1e3, 2), "us_per_call_min_rank": round(ms_min * 1e3, 2),
+            "TB_s_aggregate": round(bytes_total / (ms_max * 1e-3) / 1e12, 4),
+            "frac_of_measured_hbm_per_gpu": round(bytes_total / world / (ms_max * 1e-3) / 1e9 / peak_gbs, 4),
+            "kv_bytes_total": int(bytes_total), "kv_bytes_rank_max_over_min": round(bytes_max / bytes_min, 4),
+            "gather_to_rank0_ms": None if gather_ms is None else round(gather_ms, 3),
+            "launcher": "pad_b200.sharded.ShardedDecoder.decode (CUDA-graph replay), local permuted pools",
+            "check": {"sampled_sequences_per_rank": int(len(idx)), "max_abs_err_vs_oracle": e[0].item(),
+                      "within_tolerance": e[1].item() == 0.0, "tolerance": "2e-3 + 1e-2*|ref|"}}
+
+
+# ------------------------------------------------------------------ our arm
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -440,69 +588,97 @@ def run_ours(args):
 
     with ClockSampler(local) as clk:
         ms = time_device(pools, args.steps, args.warmup, torch, barrier)
-    t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+    t = torch.tensor([ms, per_step_bytes], device="cuda", dtype=torch.float64)
     if world > 1:
+        tb = t.clone()
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+        dist.all_reduce(tb, op=dist.ReduceOp.SUM)
+        total_bytes = tb[1].item()
+    else:
+        total_bytes = per_step_bytes
+    ms = float(t[0].item())
     ms_per_step = ms / args.steps
-    value = world * per_step_bytes * args.steps / (ms * 1e-3) / 1e12
+    value = total_bytes * args.steps / (ms * 1e-3) / 1e12
     clocks = clk.summary()
     peak_gbs, peak_kind = peaks()
     achieved_gbs = per_step_bytes / (ms_per_step * 1e-3) / 1e9
     traffic = committed_traffic() if cfg == "c2" and batch == 64 else None
 
     extra = {}
-    if cfg == "c5" and not args.no_extras:
-        extra.update(check_and_gather(pools[0], world, rank, torch))
     if args.no_extras:
         args.no_sweep = True
-    if rank == 0 and not args.no_extras:
-        e2e_ms, h2d, d2h = time_e2e(pools[0], 10, torch)
-        res_ms, rh2d, rd2h = time_e2e_resident(pools[0], 200, torch)
-        extra["e2e"] = {"value": per_step_bytes / (e2e_ms * 1e-3) / 1e12, "unit": "TB/s",
-                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms}
-        extra["e2e_kv_resident"] = {"value": per_step_bytes / (res_ms * 1e-3) / 1e12, "unit": "TB/s",
-                                    "h2d_bytes_per_step": rh2d, "d2h_bytes_per_step": rd2h,
-                                    "us_per_call": res_ms * 1e3}
-        if world == 1:
-            extra["cpu_baseline"] = cpu_baseline_sample(pools[0])
-    if not args.no_sweep and world == 1 and args.workload == "c2":
+    else:
+        e2e_ms, h2d, d2h = time_e2e(pools[0], 10 if per_step_bytes < 4e9 else 3, torch, barrier)
+        te = torch.tensor([e2e_ms], device="cuda", dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        extra["e2e"] = {"value": total_bytes / (te.item() * 1e-3) / 1e12, "unit": "TB/s",
+                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": te.item(),
+                        "path": "pinned host -> device copies of q, k_cache, v_cache, block_table, seq_lens; "
+                                "pad_b200.paged_attention_decode_cuda_v4; device -> host copy of out"}
+        if rank == 0:
+            res_ms, rh2d, rd2h = time_e2e_resident(pools[0], 200, torch)
+            extra["e2e_kv_resident"] = {"value": per_step_bytes / (res_ms * 1e-3) / 1e12, "unit": "TB/s",
+                                        "h2d_bytes_per_step": rh2d, "d2h_bytes_per_step": rd2h,
+                                        "us_per_call": res_ms * 1e3}
+            extra["host_us_per_call"] = host_us_per_call(pools[0], torch)
         del pools
         torch.cuda.empty_cache()
+        extra["c5_strong"] = c5_strong(world, rank, local, torch, barrier, peak_gbs)
+        torch.cuda.empty_cache()
+        if rank == 0 and world == 1:
+            extra.update(cpu_baselines(cfg, batch, seq_len, seq_lens))
+    if not args.no_sweep and world == 1 and args.workload == "c2":
         sweep = {}
         for b in (1, 2, 4, 8, 16, 32, 64):
             pl, nb = make_pools("c2", b, 4096, None, "cuda", 2.5 * L2_BYTES)
-            m = time_device(pl, 1000, 10, torch, barrier) / 1000
-            sweep[str(b)] = {"us_per_call": round(m * 1e3, 3), "TB_s": round(nb / (m * 1e-3) / 1e12, 4),
-                             "frac_of_measured_hbm": round(nb / (m * 1e-3) / 1e9 / peak_gbs, 4)}
+            sweep[str(b)] = rate(nb, time_device(pl, 1000, 10, torch, barrier) / 1000, peak_gbs)
             del pl
         extra["sweep_c2_seq4096"] = sweep
+        pl, nb = make_pools("c2", 64, 4096, None, "cuda", 2.5 * L2_BYTES, table_width=512)
+        extra["c2_b64_wide_table"] = dict(rate(nb, time_device(pl, 1000, 10, torch, barrier) / 1000, peak_gbs),
+                                          block_table_width=512, pages_used_per_sequence=256)
+        del pl
         lc = {}
         for sl_ in (8192, 32768, 131072):
             pl, nb = make_pools("c3", 1, sl_, None, "cuda", 2.5 * L2_BYTES)
-            m = time_device(pl, 1000, 10, torch, barrier) / 1000
-            lc[str(sl_)] = {"us_per_call": round(m * 1e3, 3), "TB_s": round(nb / (m * 1e-3) / 1e12, 4),
-                            "frac_of_measured_hbm": round(nb / (m * 1e-3) / 1e9 / peak_gbs, 4)}
+            lc[str(sl_)] = rate(nb, time_device(pl, 1000, 10, torch, barrier) / 1000, peak_gbs)
             del pl
         extra["long_context_c3_batch1"] = lc
+        sw = {}
+        for b in (1, 4):
+            pl, nb = make_pools("c3", b, 32768, None, "cuda", 2.5 * L2_BYTES)
+            row = {}
+            for s in (1, 2, 4, 8, 16, 32, 64, None):
+                m = time_device(pl, 500, 10, torch, barrier, num_splits=s) / 500
+                row["heuristic" if s is None else str(s)] = dict(
+                    rate(nb, m, peak_gbs), partitions=pad_b200.partitions(local, b, 2, 6, 128, 32, 1024, s))
+            sw[f"batch{b}"] = row
+            del pl
+        extra["num_splits_sweep_c3"] = dict(sw, seq_len=32768)
+        pl, nb = make_pools("c4", 256, None, None, "cuda", 2.5 * L2_BYTES)
+        extra["c4_llama8b_b256"] = dict(rate(nb, time_device(pl, 200, 10, torch, barrier) / 200, peak_gbs),
+                                        kv_bytes=nb)
+        del pl
+        torch.cuda.empty_cache()
         extra["same_box_reference_gpu"] = reference_gpu_comparator(torch, barrier, peak_gbs)
         extra["same_box_flashinfer"] = flashinfer_comparator(torch, barrier, peak_gbs)
 
     if rank == 0:
         line = {
-            "metric": "decode-attn achieved KV HBM TB/s (Qwen2.5-1.5B shape, seq 4096, batch 64)"
-            if args.workload == "c2" else f"decode-attn achieved KV HBM TB/s ({args.workload})",
+            "metric": metric_name(args.workload),
             "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_per_step, "us_per_call": ms_per_step * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16 in / f32 accumulate", "data": "synthetic",
-            "config": {"workload": f"{cfg} batch={batch} per GPU" + (f" seq={seq_len}" if seq_len else ""),
-                       "heads_q_kv": [hq, hkv], "head_dim": d, "page_size": ps, "pages": "random permutation",
-                       "partitions_per_gpu": parts, "l2": f"inputs rotated over {npools} KV pools totalling > 2.5x L2", "parallelism": f"batch-sharded x{world}, no collective"},
+            "config": workload_config(args.workload, world),
+            "setup": {"partitions_per_gpu": parts, "kv_pools_rotated": npools,
+                      "batch_per_gpu": batch},
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peak_gbs, "unit": "GB/s",
                          "frac": achieved_gbs / peak_gbs, "traffic": traffic,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6650 GB/s",
-                         "kernel_time": "whole step (decode_stream_kernel + merge_kernel) per call"},
+                         "kernel_time": "whole step (decode_stream_kernel + merge_kernel) per call",
+                         "traffic_source": "ncu dram bytes per decode launch, profiles/decode_stream_kernel_c2_b64.md"},
             "clocks": clocks,
             "gpu_launches": args.steps * (2 if parts > 1 else 1),
         }
@@ -512,44 +688,27 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------------------ reference arm
 def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import oracle
-    from pad_b200.cases import CONFIGS, config_case, kv_bytes
+    cfg, batch, seq_len, seq_lens = workload_spec(args.workload, world, 0)
+    if cfg == "c5":  # the reference arm samples the whole 1024-sequence batch
+        from pad_b200.cases import config_seq_lens
 
-    cfg, batch, seq_len, seq_lens = workload_spec(args.workload, 1, 0)
-    hq, hkv, d, ps, _ = CONFIGS[cfg]
-    c = config_case(cfg, batch=batch, seq_len=seq_len, seq_lens=seq_lens)
-    q, k, v = (a.astype(np.float16) for a in (c.q, c.k_cache, c.v_cache))
-    threads = oracle.max_threads()
-    # bounded sample: as many sequences as keep one step near 1 s
-    t0 = time.perf_counter()
-    oracle.decode_c(q[:1], k, v, c.block_table[:1], c.seq_lens[:1], nthreads=threads)
-    dt = max(time.perf_counter() - t0, 1e-4)
-    take = max(1, min(batch, int(1.0 / dt)))
-    for _ in range(min(args.warmup, 3)):
-        oracle.decode_c(q[:take], k, v, c.block_table[:take], c.seq_lens[:take], nthreads=threads)
-    steps = min(args.steps, 30)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        oracle.decode_c(q[:take], k, v, c.block_table[:take], c.seq_lens[:take], nthreads=threads)
-    el = time.perf_counter() - t0
-    nbytes = kv_bytes(c.seq_lens[:take], hkv, d)
-    value = nbytes * steps / el / 1e12
-    sample = (f"{take} of {batch} sequences per step, {steps} steps; C restatement of src/reference.py "
-              f"(oracle/pa_oracle.c) on {threads} host threads")
+        seq_lens = config_seq_lens("c5")
+    steps_cap = max(1, min(args.steps, 20))
+    value, desc, steps, step_ms, kind, threads = cpu_sample(cfg, batch, seq_len, seq_lens, 20.0,
+                                                            steps_cap=steps_cap, warmup=min(args.warmup, 3))
     print(json.dumps({
-        "impl": "reference", "metric": "decode-attn achieved KV HBM TB/s (Qwen2.5-1.5B shape, seq 4096, batch 64)"
-        if args.workload == "c2" else f"decode-attn achieved KV HBM TB/s ({args.workload})",
+        "impl": "reference", "metric": metric_name(args.workload),
         "value": value, "unit": "TB/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
-        "ms_per_step": el / steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{cfg} batch={batch}" + (f" seq={seq_len}" if seq_len else ""),
-                   "heads_q_kv": [hq, hkv], "head_dim": d, "page_size": ps},
-        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": threads, "kind": "port", "sample": sample},
+        "config": workload_config(args.workload, world),
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": threads, "kind": kind, "sample": desc},
         "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 

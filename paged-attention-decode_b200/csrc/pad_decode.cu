@@ -253,6 +253,54 @@ int encode_map(CUtensorMap* map, const void* base, int rank, const cuuint64_t* d
   return PAD_OK;
 }
 
+// Encoded maps of recent calls, per thread: a serving loop passes the same
+// KV caches (and often the same q buffer) every step, so most calls reuse an
+// encoding instead of paying for cuTensorMapEncodeTiled again.
+struct MapKey {
+  const void* base;
+  int rank;
+  int swz;
+  cuuint64_t dims[5];
+  cuuint64_t strides[4];
+  cuuint32_t box[5];
+};
+struct MapCacheEntry {
+  MapKey key;
+  CUtensorMap map;
+  bool valid;
+};
+constexpr int kMapCacheSize = 16;
+thread_local MapCacheEntry t_maps[kMapCacheSize];
+thread_local int t_map_next = 0;
+
+int encode_map_cached(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims,
+                      const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapSwizzle swz, const char* what) {
+  MapKey k;
+  std::memset(&k, 0, sizeof(k));
+  k.base = base;
+  k.rank = rank;
+  k.swz = (int)swz;
+  for (int i = 0; i < rank; ++i) {
+    k.dims[i] = dims[i];
+    k.box[i] = box[i];
+    if (i + 1 < rank) k.strides[i] = strides_bytes[i];
+  }
+  for (int i = 0; i < kMapCacheSize; ++i) {
+    if (t_maps[i].valid && std::memcmp(&t_maps[i].key, &k, sizeof(k)) == 0) {
+      *map = t_maps[i].map;
+      return PAD_OK;
+    }
+  }
+  const int st = encode_map(map, base, rank, dims, strides_bytes, box, swz, what);
+  if (st != PAD_OK) return st;
+  MapCacheEntry& e = t_maps[t_map_next];
+  t_map_next = (t_map_next + 1) % kMapCacheSize;
+  e.key = k;
+  e.map = *map;
+  e.valid = true;
+  return PAD_OK;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
@@ -387,14 +435,14 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, const i
                               (cuuint64_t)k_strides[0] * 2};
     const cuuint64_t vs[3] = {(cuuint64_t)v_strides[1] * 2, (cuuint64_t)v_strides[2] * 2,
                               (cuuint64_t)v_strides[0] * 2};
-    if ((st = encode_map(&prm.tm_k, k_cache, 4, dims, ks, box, swz, "k_cache")) != PAD_OK) return st;
-    if ((st = encode_map(&prm.tm_v, v_cache, 4, dims, vs, box, swz, "v_cache")) != PAD_OK) return st;
+    if ((st = encode_map_cached(&prm.tm_k, k_cache, 4, dims, ks, box, swz, "k_cache")) != PAD_OK) return st;
+    if ((st = encode_map_cached(&prm.tm_v, v_cache, 4, dims, vs, box, swz, "v_cache")) != PAD_OK) return st;
   }
   {
     const cuuint64_t dims[3] = {(cuuint64_t)head_dim, (cuuint64_t)num_q_heads, (cuuint64_t)batch};
     const cuuint32_t box[3] = {(cuuint32_t)(in.segw / 2), (cuuint32_t)(gqa * in.hg), 1u};
     const cuuint64_t qs[2] = {(cuuint64_t)q_strides[1] * 2, (cuuint64_t)q_strides[0] * 2};
-    if ((st = encode_map(&prm.tm_q, q, 3, dims, qs, box, swz, "q")) != PAD_OK) return st;
+    if ((st = encode_map_cached(&prm.tm_q, q, 3, dims, qs, box, swz, "q")) != PAD_OK) return st;
   }
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   prm.block_table = block_table;

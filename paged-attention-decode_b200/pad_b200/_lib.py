@@ -11,7 +11,7 @@ from __future__ import annotations
 import ctypes
 import os
 
-from .build import LIB_PATH
+from .build import LIB_PATH, OPS_PATH
 
 _c_i64 = ctypes.c_int64
 _c_i64p = ctypes.POINTER(ctypes.c_int64)
@@ -53,6 +53,7 @@ SIGNATURES = {
 PAD_STATIC_SCRATCH_BYTES = 16 << 20
 
 _lib = None
+_ops = None
 
 
 class PadError(RuntimeError):
@@ -76,6 +77,22 @@ def load() -> ctypes.CDLL:
             fn.argtypes = args
         _lib = lib
     return _lib
+
+
+def ops():
+    """torch.ops.pad_b200 -- the torch operator library over the C ABI
+    (_pad_torch_ops.so, which links libpad_b200.so). Fails loudly if it has
+    not been built."""
+    global _ops
+    if _ops is None:
+        load()
+        if not os.path.exists(OPS_PATH):
+            raise ImportError(f"{OPS_PATH} is missing: build it with `python -m pad_b200.build`")
+        import torch
+
+        torch.ops.load_library(OPS_PATH)
+        _ops = torch.ops.pad_b200
+    return _ops
 
 
 def check(status: int) -> None:

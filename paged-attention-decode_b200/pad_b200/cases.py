@@ -179,14 +179,16 @@ def config_pool_pages(name: str, seq_lens: np.ndarray, page_size: int) -> int:
 
 def config_case(name: str, *, batch: int | None = None, seq_len: int | None = None,
                 seq_lens: np.ndarray | None = None, seed: int = 0, device=None,
-                dtype: str = "fp16") -> PagedCase:
+                dtype: str = "fp16", table_width: int | None = None) -> PagedCase:
     """Build config ``name`` (c1..c5).
 
     ``device=None`` returns numpy fp32 arrays holding fp16-rounded values;
     a torch device returns torch tensors generated on that device in fp16
     (``dtype="fp16"``) -- this is how the multi-GB configs are made without
     a host copy. ``seq_lens`` overrides the config's own lengths (used by the
-    sharded launcher, which hands each rank its slice).
+    sharded launcher, which hands each rank its slice). ``table_width`` makes
+    the block table that many columns wide (a serving engine's table is wider
+    than the current lengths); the extra columns hold page 0.
     """
     hq, hkv, d, ps, std = CONFIGS[name]
     if seq_lens is None:
@@ -194,7 +196,7 @@ def config_case(name: str, *, batch: int | None = None, seq_len: int | None = No
     seq_lens = np.asarray(seq_lens, dtype=np.int32)
     num_pages = max(config_pool_pages(name, seq_lens, ps), 1)
     rng = np.random.default_rng(1000 + seed)
-    bt = permuted_block_table(seq_lens, ps, num_pages, rng, hole_fill="zero")
+    bt = permuted_block_table(seq_lens, ps, num_pages, rng, hole_fill="zero", max_pages=table_width)
     b = len(seq_lens)
     if device is None:
         k = _normal_fp16_as_fp32(rng, (num_pages, ps, hkv, d), std)

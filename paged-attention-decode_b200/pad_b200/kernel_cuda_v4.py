@@ -14,9 +14,12 @@ Differences, by design:
     fixed 64; an explicit ``num_splits=S`` launches ``S * batch * Hkv``
     partitions, i.e. S splits per (sequence, KV head) pair for uniform
     batches, exactly as the reference's grid.z = S did.
-  * The launch goes to the current torch stream of ``q``'s device.
-  * Argument errors the native library detects raise ``PadError``
-    (a RuntimeError, like the reference's TORCH_CHECK).
+  * The call goes through the torch operator ``torch.ops.pad_b200.decode``
+    (csrc/pad_torch_op.cpp, host C++ over the C ABI of libpad_b200.so), which
+    launches on the current torch stream of ``q``'s device and keeps one
+    reusable workspace per (device, stream).
+  * Argument errors the native library detects raise RuntimeError (the
+    operator's TORCH_CHECK, like the reference's, cuda/kernel_v4_split_k.cu:216-223).
   * With ``PAD_B200_CHECK=1`` in the environment the call synchronises and
     raises ValueError for invalid block-table page ids or out-of-range
     seq_lens -- the value checks of the reference oracle
@@ -33,34 +36,11 @@ import torch
 from . import _lib
 
 _SUPPORTED_HEAD_DIMS = (16, 32, 64, 128)
+_OPS = _lib.ops()
 _CHECK_VALUES = os.environ.get("PAD_B200_CHECK", "0") not in ("", "0")
 
 
-class _DeviceState:
-    """Per (device, stream) reusable workspace and error-flag word."""
-
-    def __init__(self, device: torch.device):
-        self.device = device
-        self.workspace = torch.empty(0, dtype=torch.uint8, device=device)
-        self.flags = torch.zeros(1, dtype=torch.int32, device=device)
-
-    def workspace_ptr(self, nbytes: int) -> int:
-        if self.workspace.numel() < nbytes:
-            self.workspace = torch.empty(max(nbytes, 2 * self.workspace.numel()), dtype=torch.uint8,
-                                         device=self.device)
-        return self.workspace.data_ptr()
-
-
-_STATE: dict[tuple[int, int], _DeviceState] = {}
 _WS_CACHE: dict[tuple, int] = {}
-
-
-def _state(device: torch.device, stream: int) -> _DeviceState:
-    key = (device.index, stream)
-    st = _STATE.get(key)
-    if st is None:
-        st = _STATE[key] = _DeviceState(device)
-    return st
 
 
 def workspace_bytes(device_index: int, batch: int, num_kv_heads: int, gqa_ratio: int, head_dim: int,
@@ -126,51 +106,24 @@ def paged_attention_decode_cuda_v4(
     assert block_table.dim() == 2 and block_table.shape[0] == batch, "block_table must be [B, max_pages]"
     assert seq_lens.dim() == 1 and seq_lens.shape[0] == batch, "seq_lens must be [B]"
     assert num_splits is None or num_splits >= 1, "num_splits must be >= 1"
-    gqa_ratio = num_q_heads // num_kv_heads
-
-    dev = q.device
-    block_table = block_table.to(device=dev, dtype=torch.int32)
-    if block_table.stride(1) != 1:
-        block_table = block_table.contiguous()
-    seq_lens = seq_lens.to(device=dev, dtype=torch.int32).contiguous()
+    assert out is None or (out.shape == q.shape and out.dtype == torch.float16), "bad out tensor"
     scale = scale if scale is not None else 1.0 / math.sqrt(head_dim)
-    if q.stride(2) != 1 or q.stride(0) % 8 or q.stride(1) % 8 or q.data_ptr() % 16:
-        q = q.contiguous()
-    if out is None:
-        out = torch.empty((batch, num_q_heads, head_dim), dtype=torch.float16, device=dev)
-    else:
-        assert out.shape == q.shape and out.dtype == torch.float16 and out.device == dev, "bad out tensor"
-    if batch == 0:
-        return out
-
-    with torch.cuda.device(dev):
-        stream = torch.cuda.current_stream(dev).cuda_stream
-        st = _state(dev, stream)
-        splits = 0 if num_splits is None else int(num_splits)
-        max_pages = block_table.shape[1]
-        nbytes = workspace_bytes(dev.index, batch, num_kv_heads, gqa_ratio, head_dim, page_size, max_pages, splits)
-        ws = st.workspace_ptr(nbytes)
-        lib = _lib.load()
-        if _CHECK_VALUES:
-            st.flags.zero_()
-        _lib.check(lib.pad_paged_attention_decode(
-            q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_table.data_ptr(), seq_lens.data_ptr(),
-            out.data_ptr(), batch, num_q_heads, num_kv_heads, head_dim, num_pages, page_size, max_pages,
-            _lib.i64_array(q.stride()), _lib.i64_array(k_cache.stride()), _lib.i64_array(v_cache.stride()),
-            block_table.stride(0), _lib.i64_array(out.stride()), float(scale), splits, ws, st.workspace.numel(),
-            stream, st.flags.data_ptr()))
-        if _CHECK_VALUES:
-            _raise_for_flags(int(st.flags.item()))
+    if _CHECK_VALUES:
+        read_error_flags(q.device)
+    out = _OPS.decode(q, k_cache, v_cache, block_table, seq_lens, 0 if num_splits is None else int(num_splits),
+                      float(scale), out)
+    if _CHECK_VALUES:
+        _raise_for_flags(read_error_flags(q.device))
     return out
 
 
 def read_error_flags(device: torch.device | None = None, reset: bool = True) -> int:
     """PAD_FLAG_* bits the kernels raised on ``device``'s current stream since the last reset (syncs)."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    st = _state(dev, torch.cuda.current_stream(dev).cuda_stream)
-    v = int(st.flags.item())
+    flags = _OPS.error_flags(dev.index)
+    v = int(flags.item())
     if reset:
-        st.flags.zero_()
+        flags.zero_()
     return v
 
 
@@ -217,37 +170,11 @@ def paged_attention_decode_csr(
     assert num_q_heads % num_kv_heads == 0, "num_q_heads must be divisible by num_kv_heads (GQA)"
     assert head_dim in _SUPPORTED_HEAD_DIMS, f"head_dim must be one of {_SUPPORTED_HEAD_DIMS}"
     assert kv_indptr.shape == (batch + 1,) and kv_last_page_len.shape == (batch,), "bad CSR shapes"
-    dev = q.device
-    indptr = kv_indptr.to(device=dev, dtype=torch.int32).contiguous()
-    indices = kv_indices.to(device=dev, dtype=torch.int32).contiguous()
-    last = kv_last_page_len.to(device=dev, dtype=torch.int32).contiguous()
     scale = scale if scale is not None else 1.0 / math.sqrt(head_dim)
-    if q.stride(2) != 1 or q.stride(0) % 8 or q.stride(1) % 8 or q.data_ptr() % 16:
-        q = q.contiguous()
-    if out is None:
-        out = torch.empty((batch, num_q_heads, head_dim), dtype=torch.float16, device=dev)
-    if batch == 0:
-        return out
-    nnz = max(int(indices.numel()), 1)
-    if indices.numel() == 0:
-        indices = torch.zeros(1, dtype=torch.int32, device=dev)
-    with torch.cuda.device(dev):
-        stream = torch.cuda.current_stream(dev).cuda_stream
-        st = _state(dev, stream)
-        splits = 0 if num_splits is None else int(num_splits)
-        lib = _lib.load()
-        need = _lib.ctypes.c_size_t(0)
-        _lib.check(lib.pad_decode_csr_workspace_bytes(dev.index, batch, num_kv_heads, num_q_heads // num_kv_heads,
-                                                      head_dim, page_size, nnz, splits, _lib.ctypes.byref(need)))
-        ws = st.workspace_ptr(int(need.value))
-        _lib.check(lib.pad_paged_attention_decode_csr(
-            q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), indptr.data_ptr(), indices.data_ptr(),
-            last.data_ptr(), out.data_ptr(), batch, num_q_heads, num_kv_heads, head_dim, num_pages, page_size, nnz,
-            _lib.i64_array(q.stride()), _lib.i64_array(k_cache.stride()), _lib.i64_array(v_cache.stride()),
-            _lib.i64_array(out.stride()), float(scale), splits, ws, st.workspace.numel(), stream,
-            st.flags.data_ptr()))
-        if _CHECK_VALUES:
-            _raise_for_flags(int(st.flags.item()))
+    out = _OPS.decode_csr(q, k_cache, v_cache, kv_indptr, kv_indices, kv_last_page_len,
+                          0 if num_splits is None else int(num_splits), float(scale), out)
+    if _CHECK_VALUES:
+        _raise_for_flags(read_error_flags(q.device))
     return out
 
 
@@ -260,20 +187,6 @@ def paged_kv_append(k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Ten
     batch, hkv, d = k_new.shape
     num_pages, page_size, cache_hkv, cache_d = k_cache.shape
     assert (cache_hkv, cache_d) == (hkv, d), "k_new must be [B, Hkv, D] matching the cache"
-    dev = k_cache.device
-    bt = block_table.to(device=dev, dtype=torch.int32)
-    if bt.stride(1) != 1:
-        bt = bt.contiguous()
-    pos = positions.to(device=dev, dtype=torch.int32).contiguous()
-    k_new = k_new if k_new.stride(2) == 1 else k_new.contiguous()
-    v_new = v_new if v_new.stride(2) == 1 else v_new.contiguous()
-    with torch.cuda.device(dev):
-        stream = torch.cuda.current_stream(dev).cuda_stream
-        st = _state(dev, stream)
-        _lib.check(_lib.load().pad_paged_kv_append(
-            k_new.data_ptr(), v_new.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), bt.data_ptr(), pos.data_ptr(),
-            batch, hkv, d, num_pages, page_size, bt.shape[1], _lib.i64_array(k_new.stride()),
-            _lib.i64_array(v_new.stride()), _lib.i64_array(k_cache.stride()), _lib.i64_array(v_cache.stride()),
-            bt.stride(0), stream, st.flags.data_ptr()))
-        if _CHECK_VALUES:
-            _raise_for_flags(int(st.flags.item()))
+    _OPS.kv_append(k_new, v_new, k_cache, v_cache, block_table, positions)
+    if _CHECK_VALUES:
+        _raise_for_flags(read_error_flags(k_cache.device))
