@@ -6,9 +6,15 @@ parameters are used as loaded; with equal but shorter lengths the cursor has a
 closed form; anything else (ragged lengths, an empty sequence, more than 256
 sequences, a CSR index) takes the scan hand-off. The merge kernel guesses its
 split descriptors for full rows and folds again when the descriptor differs.
-Each case here lands on one of those paths, with the heuristic split count and
-an explicit one, and is checked against the C oracle.
+With at most 16 (sequence, KV-head group) pairs the split pairs are merged
+inside the decode kernel instead (arrival counters in the workspace, the last
+CTAs to arrive fold). Each case here lands on one of those paths, with the
+heuristic split count and an explicit one, and is checked against the C oracle.
 """
+
+import os
+import subprocess
+import sys
 
 import numpy as np
 import pytest
@@ -76,3 +82,67 @@ def test_guess_miss_after_guess_hit_on_one_workspace():
         ref = oracle.decode_c(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens)
         out = paged_attention_decode_cuda_v4(*to_gpu(c)).float().cpu().numpy()
         assert_parity(out, ref, f"seq={int(c.seq_lens[0])}")
+
+
+def _abi_decode(c, ws, num_splits=0):
+    """One decode through the C ABI with a caller-owned workspace."""
+    from pad_b200 import _lib
+
+    q, k, v, bt, sl = to_gpu(c)
+    out = torch.empty_like(q)
+    _lib.check(_lib.load().pad_paged_attention_decode(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), bt.data_ptr(), sl.data_ptr(), out.data_ptr(), q.shape[0],
+        q.shape[1], k.shape[2], q.shape[2], k.shape[0], k.shape[1], bt.shape[1], _lib.i64_array(q.stride()),
+        _lib.i64_array(k.stride()), _lib.i64_array(v.stride()), bt.stride(0), _lib.i64_array(out.stride()),
+        1.0 / q.shape[2] ** 0.5, num_splits, ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream,
+        0))
+    return out
+
+
+def test_fused_merge_leaves_counters_zero_across_shapes():
+    """One zero-filled workspace shared by calls of different shapes: fused
+    (few pairs: long context, oversplit with empty partitions, ragged) and
+    unfused (many pairs). Every result matches the oracle and the counter
+    region (the first 256 bytes) is zero after every call."""
+    cases = [
+        (explicit_case([20000], num_kv_heads=2, gqa_ratio=6, head_dim=128, page_size=32, seed=51), 0),
+        (explicit_case([5], num_kv_heads=2, gqa_ratio=6, head_dim=128, page_size=16, seed=52), 64),
+        (explicit_case([3000, 17, 0, 9000], num_kv_heads=4, gqa_ratio=4, head_dim=64, page_size=16, seed=53), 0),
+        (explicit_case([300] * 40, num_kv_heads=2, gqa_ratio=6, head_dim=128, page_size=16, seed=54), 0),
+        (explicit_case([2500, 7000], num_kv_heads=8, gqa_ratio=8, head_dim=128, page_size=16, seed=55), 5),
+        (explicit_case([20000], num_kv_heads=2, gqa_ratio=6, head_dim=128, page_size=32, seed=51), 0),
+    ]
+    ws = torch.zeros(64 << 20, dtype=torch.uint8, device="cuda")
+    for i, (c, s) in enumerate(cases):
+        ref = oracle.decode_c(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens)
+        out = _abi_decode(c, ws, s)
+        torch.cuda.synchronize()
+        assert_parity(out.float().cpu().numpy(), ref, f"case {i} S={s}")
+        assert int(ws[:256].count_nonzero()) == 0, f"case {i}: counters not reset"
+
+
+_UNFUSED_SCRIPT = """
+import sys
+sys.path[:0] = {paths!r}
+import numpy as np, torch, oracle
+from gpu_utils import assert_parity, run
+from pad_b200.cases import config_case, explicit_case
+for c, s in [(config_case("c3", batch=1, seq_len=32768, seed=9), None),
+             (explicit_case([1, 17, 300, 4000], num_kv_heads=2, gqa_ratio=6, head_dim=128, page_size=16, seed=5), 3),
+             (config_case("c2", batch=8), None)]:
+    ref = oracle.decode_c(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens)
+    assert_parity(run(c, num_splits=s), ref, "unfused")
+print("ok")
+"""
+
+
+def test_few_pairs_through_the_merge_kernel_when_fusion_is_off():
+    """PAD_B200_FUSED_MERGE=0 routes few-pair batches through the separate
+    merge kernel (the A/B switch): that path stays correct too."""
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    paths = [root, os.path.join(root, "paged-attention-decode_b200"), here]
+    env = dict(os.environ, PAD_B200_FUSED_MERGE="0")
+    r = subprocess.run([sys.executable, "-c", _UNFUSED_SCRIPT.format(paths=paths)], env=env, capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-3000:]
