@@ -85,14 +85,9 @@ int pad_decode_partitions(int device, int64_t batch, int64_t num_kv_heads, int64
 
 /* Bytes of device workspace pad_paged_attention_decode needs for this
  * problem (same arguments as pad_decode_partitions). The workspace holds the
- * fp32 split partials (O, m, l), per-partition merge descriptors and, in its
- * first 256 bytes, the arrival counters of the in-kernel merge used when the
- * batch has at most 16 (sequence, KV-head group) pairs. It must be
- * zero-filled once before its first use (e.g. one cudaMemsetAsync after
- * allocating it); every call leaves it in a state the next call accepts,
- * whatever that call's shape, so it may be reused by consecutive calls on one
- * stream (calls that overlap in time must use distinct workspaces). After a
- * call that raised PAD_FLAG_WAIT_TIMEOUT, zero it again. */
+ * fp32 split partials (O, m, l) and per-partition merge descriptors; it
+ * needs no initialisation and may be reused by consecutive calls on one
+ * stream (calls that overlap in time must use distinct workspaces). */
 int pad_decode_workspace_bytes(int device, int64_t batch, int64_t num_kv_heads, int64_t gqa_ratio,
                                int64_t head_dim, int64_t page_size, int64_t max_pages_per_seq,
                                int64_t num_splits, size_t* bytes);
@@ -185,9 +180,8 @@ int pad_paged_kv_append(const void* k_new, const void* v_new, void* k_cache, voi
  * array's device address (cudaGetSymbolAddress) with that device current,
  * so make that first call before any stream capture. All calls on a device
  * share the one array: calls that overlap on the GPU (different streams, no
- * ordering between them) race and must be avoided. Each call clears the
- * part of the array that must start at zero (the in-kernel merge's counters,
- * one small memset on the stream) and rewrites everything else it reads.
+ * ordering between them) race and must be avoided. Nothing in the array has
+ * to start zeroed; each call rewrites what it reads.
  * No counterpart in the reference. */
 #define PAD_STATIC_SCRATCH_BYTES ((size_t)16 << 20)
 int pad_paged_attention_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,

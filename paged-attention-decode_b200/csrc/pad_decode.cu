@@ -7,7 +7,6 @@
 
 #include <algorithm>
 #include <cmath>
-#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -87,16 +86,7 @@ int head_group_for(int64_t hkv, int64_t gqa) {
 #define PAD_MERGE_DEEP 32
 #endif
 constexpr int64_t kMergeWide = PAD_MERGE_WIDE, kMergeDeep = PAD_MERGE_DEEP;
-
-// PAD_B200_FUSED_MERGE=0 in the environment turns the fused merge off (the
-// merge kernel then serves every split pair); read once, for A/B timing.
-bool fused_merge_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("PAD_B200_FUSED_MERGE");
-    return v == nullptr || std::strcmp(v, "0") != 0;
-  }();
-  return on;
-}
+constexpr int64_t kFewPairs = 16;  // the num_splits=None heuristic: see make_plan
 
 bool pick_instance(int64_t head_dim, int64_t gqa, int hg, bool swz, Instance* out) {
   const bool nt1 = gqa <= 8;
@@ -170,7 +160,6 @@ struct Plan {
   int box_rows = 1;
   int64_t partitions = 0;
   int64_t slots = 0;
-  bool fused = false;  // split pairs folded inside the decode kernel (no merge launch)
   size_t off_meta = 0, off_ml = 0, off_o = 0, bytes = 0;
 };
 
@@ -225,14 +214,8 @@ int make_plan(int device, int64_t batch, int64_t hkv, int64_t gqa, int64_t head_
   if (parts < 1) parts = 1;
   plan->partitions = parts;
   plan->slots = parts + batch * groups;
-  // Fused only when every CTA of the grid is resident at once: folders spin
-  // until all of their pair's partitions have arrived, which must never wait
-  // for an SM a spinning folder holds.
-  plan->fused = batch * groups <= kFewPairs && parts <= (int64_t)sms * occ && fused_merge_enabled();
-  // the fused merge's counters sit at a fixed offset in every layout, so any
-  // call may reuse a workspace another call (of any shape) left behind
-  plan->off_meta = kCounterBytes;
-  plan->off_ml = align_up(plan->off_meta + (size_t)std::max<int64_t>(parts, batch * groups) * sizeof(int4), 256);
+  plan->off_meta = 0;
+  plan->off_ml = align_up((size_t)std::max<int64_t>(parts, batch * groups) * sizeof(int4), 256);
   plan->off_o = align_up(plan->off_ml + (size_t)plan->slots * hg * gqa * sizeof(float2), 256);
   plan->bytes = align_up(plan->off_o + (size_t)plan->slots * hg * gqa * head_dim * sizeof(float), 256);
   return PAD_OK;
@@ -484,18 +467,9 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, const i
   prm.box_rows_log2 = __builtin_ctz((unsigned)plan.box_rows);
   prm.page_shift = (page_size & (page_size - 1)) == 0 ? __builtin_ctz((unsigned)page_size) : -1;
   prm.meta_by_pair = batch * (num_kv_heads / in.hg) < plan.partitions ? 1 : 0;
-  prm.fused_merge = plan.fused ? 1 : 0;
-  prm.counters = reinterpret_cast<int*>(ws);
   prm.scale_log2 = scale * kLog2e;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (static_scratch && plan.fused) {
-    // the shared scratch keeps whatever the last call left: clear the merge
-    // counters, which must start at zero (a caller's own workspace is zeroed
-    // once by its owner and left zero by every call)
-    e = cudaMemsetAsync(ws, 0, kCounterBytes, s);
-    if (e != cudaSuccess) return cuda_fail(e, "clearing the static scratch's counters");
-  }
   void* args[] = {&prm};
   {
     cudaLaunchConfig_t cfg = {};
@@ -513,7 +487,7 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, const i
     e = cudaLaunchKernelExC(&cfg, in.kernel, args);
   }
   if (e != cudaSuccess) return cuda_fail(e, "launching the decode kernel");
-  if (plan.partitions > 1 && !plan.fused) {
+  if (plan.partitions > 1) {
     const float* a0 = prm.ws_o;
     const float2* a1 = prm.ws_ml;
     const int4* a2 = prm.ws_meta;

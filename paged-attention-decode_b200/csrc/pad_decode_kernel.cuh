@@ -39,8 +39,6 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kSmemBudget = 227 * 1024;
 constexpr int kSeqCache = 1024;   // seq_lens kept in shared memory when batch <= this
 constexpr int kFastBatch = 256;   // largest batch the producer's fast start checks (8 loads per lane)
-constexpr int kFewPairs = 16;     // at most this many (sequence, head group) pairs: fused merge
-constexpr int kCounterBytes = 256;  // workspace head: the fused merge's 2 * kFewPairs counters
 
 struct __align__(64) DecodeParams {
   CUtensorMap tm_k;  // dims {D, page_size, Hkv, num_pages}, box {SEG, R, HG, 1}
@@ -65,12 +63,6 @@ struct __align__(64) DecodeParams {
   int box_rows_log2; // log2(R)
   int page_shift;    // log2(page_size) when it is a power of two, else -1
   int meta_by_pair;  // merge descriptors indexed by pair (else by partition)
-  // Fused merge (at most kFewPairs (sequence, head group) pairs): split pairs
-  // are folded inside this kernel by the last CTAs to arrive, no merge kernel.
-  // counters[pair] counts a pair's arrivals, counters[kFewPairs + pair] its
-  // finished folders; both are zero between calls.
-  int fused_merge;
-  int* counters;
   float scale_log2;  // scale * log2(e)
 };
 
@@ -166,7 +158,7 @@ struct TileDesc {
   int flags;          // kFirst | kLast | kSplit
   int slot;           // partial slot when split
   int qslot;          // query-tile ring slot of this segment
-  int pair_start;     // global index of tile 0 of the pair
+  int pad;
 };
 constexpr int kFirst = 1, kLast = 2, kSplit = 4;
 

@@ -130,149 +130,12 @@ __device__ __forceinline__ void store_page_ids(int* slot_ids, int lane, const in
     if (lane + 32 * u < TR::NB_MAX) slot_ids[lane + 32 * u] = v[u];
 }
 
-// ---- log-sum-exp folding of split partials (analysis/split_k_derivation.md:44-86):
-//   M = max_s m_s;  L = sum_s l_s 2^(m_s - M);  O = sum_s O_s 2^(m_s - M) / L
-// kept as an online state (m, l, 4 unnormalised output columns a). A
-// partial with m_s = -inf weighs 0 and its O is not used (the guard of
-// analysis/split_k_derivation.md:67-86).
-struct FoldState {
-  float m, l;
-  float4 a;
-};
-
-__device__ __forceinline__ FoldState fold_empty() { return FoldState{-INFINITY, 0.f, make_float4(0.f, 0.f, 0.f, 0.f)}; }
-
-// Fold one partial (m, l, O) into the state.
-__device__ __forceinline__ void fold_in(FoldState& st, float2 ml, float4 o) {
-  if (ml.x == -INFINITY) return;
-  const float mn = fmaxf(st.m, ml.x);
-  const float al = ex2(st.m - mn), be = ex2(ml.x - mn);
-  st.l = st.l * al + ml.y * be;
-  st.a.x = st.a.x * al + o.x * be;
-  st.a.y = st.a.y * al + o.y * be;
-  st.a.z = st.a.z * al + o.z * be;
-  st.a.w = st.a.w * al + o.w * be;
-  st.m = mn;
-}
-
-// Fold another state (m2, l2, a2) into the state; both may be empty.
-__device__ __forceinline__ void fold_state(FoldState& st, float m2, float l2, float4 a2) {
-  const float mn = fmaxf(st.m, m2), mu = (mn == -INFINITY) ? 0.f : mn;
-  const float al = ex2(st.m - mu), be = ex2(m2 - mu);
-  st.l = st.l * al + l2 * be;
-  st.a.x = st.a.x * al + a2.x * be;
-  st.a.y = st.a.y * al + a2.y * be;
-  st.a.z = st.a.z * al + a2.z * be;
-  st.a.w = st.a.w * al + a2.w * be;
-  st.m = mn;
-}
-
-// Fold the states of the lanes C4 apart in a warp (they hold the same columns).
-template <int C4>
-__device__ __forceinline__ void fold_warp(FoldState& st) {
-#pragma unroll
-  for (int o = C4; o < 32; o <<= 1) {
-    const float m2 = __shfl_xor_sync(0xffffffffu, st.m, o), l2 = __shfl_xor_sync(0xffffffffu, st.l, o);
-    float4 a2;
-    a2.x = __shfl_xor_sync(0xffffffffu, st.a.x, o);
-    a2.y = __shfl_xor_sync(0xffffffffu, st.a.y, o);
-    a2.z = __shfl_xor_sync(0xffffffffu, st.a.z, o);
-    a2.w = __shfl_xor_sync(0xffffffffu, st.a.w, o);
-    fold_state(st, m2, l2, a2);
-  }
-}
-
-// Combine NW warps' states (lanes < C4 of warp x stored theirs at red_o[x],
-// red_m[x], red_l[x]) and write 4 fp16 columns: the caller's thread tid < C4
-// handles columns 4*tid .. 4*tid+3 of its slice, at `o`.
-template <int NW, int DC>
-__device__ __forceinline__ void fold_write(const float (*red_o)[DC], const float* red_m, const float* red_l, int tid,
-                                           __half* o) {
-  float M = -INFINITY;
-#pragma unroll
-  for (int x = 0; x < NW; ++x) M = fmaxf(M, red_m[x]);
-  const float Mu = (M == -INFINITY) ? 0.f : M;
-  float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-  float L = 0.f;
-#pragma unroll
-  for (int x = 0; x < NW; ++x) {
-    const float wt = ex2(red_m[x] - Mu);  // 0 for warps that saw no partial
-    const float4 v = *reinterpret_cast<const float4*>(&red_o[x][tid * 4]);
-    t.x += v.x * wt;
-    t.y += v.y * wt;
-    t.z += v.z * wt;
-    t.w += v.w * wt;
-    L += red_l[x] * wt;
-  }
-  const float inv = L > 0.f ? 1.f / L : 0.f;
-  reinterpret_cast<__half2*>(o)[0] = __floats2half2_rn(t.x * inv, t.y * inv);
-  reinterpret_cast<__half2*>(o)[1] = __floats2half2_rn(t.z * inv, t.w * inv);
-}
-
 // Named barriers of the consumer warps (ids 1 and 2; 0 is __syncthreads).
 // Safe from deadlock because consumer warps only ever leave the tile loop
 // together: every exit decision goes through consumer_vote first.
 constexpr uint32_t kConsumerThreads = 32 * kConsumerWarps;
 __device__ __forceinline__ void consumer_sync() { named_barrier(1, kConsumerThreads); }
 __device__ __forceinline__ bool consumer_vote(bool ok) { return named_barrier_and(2, kConsumerThreads, ok); }
-
-// Bounded wait until the counter at `c` reaches `target` (acquire: what the
-// arrivals released is visible afterwards). False after kWaitTimeoutNs.
-__device__ __noinline__ bool wait_count_bounded(const int* c, int target) {
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 0;; ++it) {
-    if (ld_acquire_gpu(c) >= target) return true;
-    if ((it & 63u) == 63u && globaltimer_ns() - t0 > kWaitTimeoutNs) return false;
-  }
-}
-
-// Fused merge: the consumer warps of one CTA fold the partial slots
-// [s0, s0 + ns) of query row y of a pair, columns [z * DC, (z + 1) * DC) (DC =
-// 32, or D below 64), and write them as fp16 at `o` (that row's output from
-// column z * DC). Partials come from other CTAs of this grid: L2 loads after
-// the acquire on the pair's counter. `red` is shared scratch of
-// kConsumerWarps * (DC + 2) floats.
-template <int D>
-__device__ __noinline__ void fold_slice(const DecodeParams& p, int s0, int ns, int rows, int y, int z, __half* o,
-                                        float* red) {
-  constexpr int DS = D >= 64 ? D / 32 : 1, DC = D / DS, C4 = DC / 4, PG = kConsumerThreads / C4, UNR = 4;
-  constexpr int NW = kConsumerWarps;
-  float (*red_o)[DC] = reinterpret_cast<float (*)[DC]>(red);
-  float* red_m = red + NW * DC;
-  float* red_l = red_m + NW;
-  const int tid = threadIdx.x;
-  const int c = tid % C4 + z * C4, sg = tid / C4;
-  FoldState st = fold_empty();
-  for (int s = sg; s < ns; s += UNR * PG) {
-    float2 ml[UNR];
-    float4 v[UNR];
-#pragma unroll
-    for (int u = 0; u < UNR; ++u) {
-      const int su = s + u * PG;
-      ml[u] = make_float2(-INFINITY, 0.f);
-      v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (su < ns) {
-        const int64_t row = (int64_t)(s0 + su) * rows + y;
-        ml[u] = ld_cg_f2(p.ws_ml + row);
-        v[u] = ld_cg_f4(p.ws_o + row * D + 4 * c);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < UNR; ++u) fold_in(st, ml[u], v[u]);
-  }
-  fold_warp<C4>(st);
-  const int wid = tid >> 5, lid = tid & 31;
-  if (lid < C4) {
-    *reinterpret_cast<float4*>(&red_o[wid][lid * 4]) = st.a;
-    if (lid == 0) {
-      red_m[wid] = st.m;
-      red_l[wid] = st.l;
-    }
-  }
-  consumer_sync();
-  if (tid < C4) fold_write<NW, DC>(red_o, red_m, red_l, tid, o + 4 * tid);
-  consumer_sync();
-}
 
 template <class TR>
 __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid_constant__ DecodeParams p) {
@@ -424,14 +287,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
       if (c.b >= 0) c.base = row_base(p, c.b);
     }
     const int ntiles = t1 - t0;
-    if (lane == 0 && !p.meta_by_pair && !p.fused_merge) p.ws_meta[w] = make_int4(-1, 0, 0, 0);
+    if (lane == 0 && !p.meta_by_pair) p.ws_meta[w] = make_int4(-1, 0, 0, 0);
     if (lane == 0) PAD_STAMP(7);
     if (ntiles <= 0) {
       // An empty partition (more partitions than tiles) can sit between the
       // first and last partition of a split pair; it owns a partial slot of
-      // that pair, which it marks empty (m = -inf, l = 0) for every head. (In
-      // a fused merge the consumer warps do this and arrive for it.)
-      if (c.b >= 0 && c.pair_start < t0 && !p.fused_merge) {
+      // that pair, which it marks empty (m = -inf, l = 0) for every head.
+      if (c.b >= 0 && c.pair_start < t0) {
         const int slot = c.b * ngroups + c.hg + w;
         for (int x = lane; x < HG * G; x += 32) p.ws_ml[(int64_t)slot * HG * G + x] = make_float2(-INFINITY, 0.f);
       }
@@ -528,12 +390,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
         // are disjoint across pairs and stay below partitions + pairs.
         dsc.slot = pair + w;
         dsc.qslot = qs;
-        dsc.pair_start = c.pair_start;
+        dsc.pad = 0;
         descs[s] = dsc;
         mbar_arrive(&full[s]);
         // The partition holding a pair's first tile publishes its merge
         // descriptor (indexed by pair or by partition, see meta_by_pair).
-        if (c.i == 0 && (split || p.meta_by_pair) && !p.fused_merge) {
+        if (c.i == 0 && (split || p.meta_by_pair)) {
           const int last_owner = part_owner((int64_t)c.pair_start + c.n - 1, total, W);
           p.ws_meta[p.meta_by_pair ? pair : w] =
               split ? make_int4(pair, pair + w, last_owner - w + 1, 1) : make_int4(-1, 0, 0, 0);
@@ -585,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
   // ---- exclusive scan of tiles per sequence (x head groups) over the
   // consumer threads: this partition's tile range, its first cursor (handed
   // to the producer when it cannot use the fast start) and the seq_lens cache.
-  int t0, t1, ntiles, total_tiles;
+  int t0, t1, ntiles;
   {
     const int per = (p.batch + kConsumerThreads - 1) / kConsumerThreads;
     const int b_lo = min(p.batch, tid * per), b_hi = min(p.batch, b_lo + per);
@@ -615,7 +477,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
       total += v;
     }
     if (bad && w == 0) raise_flag(p, PAD_FLAG_SEQ_LEN_RANGE);
-    total_tiles = total;
     t0 = total > 0 ? part_begin(w, total, W) : 0;
     t1 = total > 0 ? part_begin(w + 1, total, W) : 0;
     if (t0 < total && excl <= t0 && t0 < excl + local) {
@@ -651,7 +512,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     // (only when the scan saw one: no extra global reads on the common path)
     for (int b = w; any_empty && b < p.batch; b += (int)W) {
       if (seq_of(p, sseq, b, cap) == 0) {
-        if (p.meta_by_pair && !p.fused_merge && tid < ngroups) p.ws_meta[b * ngroups + tid] = make_int4(-1, 0, 0, 0);
+        if (p.meta_by_pair && tid < ngroups) p.ws_meta[b * ngroups + tid] = make_int4(-1, 0, 0, 0);
         const int hq = p.hkv * G;
 #pragma unroll 1
         for (int x = tid; x < hq * (D / 2); x += kConsumerThreads) {
@@ -662,31 +523,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     }
   }
   ntiles = t1 - t0;
-  // Fused merge bookkeeping: the split pairs this CTA arrived for (at most
-  // two: its first and its last segment), {pair, first slot, slots, -} in
-  // shared memory, the tickets (arrival order) in thread 0's registers.
-  int* pend = scan + 48;
-  int npend = 0, tk0 = 0, tk1 = 0;
-  if (ntiles <= 0) {
-    if (!p.fused_merge) return;
-    // An empty partition inside a split pair owns a slot of it: mark it empty
-    // (m = -inf, l = 0) and arrive like the pair's other partitions.
-    consumer_sync();  // the scan's cursor (cur_smem) is visible
-    if (!(cur_smem[0] >= 0 && cur_smem[5] < t0)) return;
-    const int pair = cur_smem[0] * ngroups + cur_smem[1];
-    for (int x = tid; x < HG * G; x += kConsumerThreads)
-      p.ws_ml[(int64_t)(pair + w) * HG * G + x] = make_float2(-INFINITY, 0.f);
-    consumer_sync();
-    if (tid == 0) {
-      const int fo = part_owner(cur_smem[5], total_tiles, W);
-      const int lo = part_owner((int64_t)cur_smem[5] + cur_smem[3] - 1, total_tiles, W);
-      pend[0] = pair;
-      pend[1] = pair + fo;
-      pend[2] = lo - fo + 1;
-      tk0 = atom_add_release_gpu(p.counters + pair, 1);
-      npend = 1;
-    }
-  }
+  if (ntiles <= 0) return;
   const int hl = warp / WPH;               // local KV head this warp serves
   const uint32_t t_base = (warp % WPH) * 16;  // its 16 tokens within the tile
   const int lr = p.box_rows_log2;
@@ -1002,60 +839,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
         // No trailing sync: the next epilogue's first sync orders these reads
         // before any warp writes the buffer again.
       }
-      if (split && p.fused_merge) {
-        consumer_sync();  // every warp's partial stores precede the release below
-        if (tid == 0) {
-          const int pair = dsc.b * ngroups + dsc.hg;
-          const int fo = part_owner(dsc.pair_start, total_tiles, W);
-          const int lo = part_owner((int64_t)dsc.pair_start + tiles_of<TR>(dsc.seq) - 1, total_tiles, W);
-          pend[4 * npend + 0] = pair;
-          pend[4 * npend + 1] = pair + fo;
-          pend[4 * npend + 2] = lo - fo + 1;
-          // the ticket is first used after the tile loop: no stall here
-          if (npend == 0) tk0 = atom_add_release_gpu(p.counters + pair, 1);
-          else tk1 = atom_add_release_gpu(p.counters + pair, 1);
-          ++npend;
-        }
-      }
-    }
-  }
-  if (p.fused_merge) {
-    // ---- fused merge: a split pair with N arrivals has K = min(N, slices)
-    // folders, its last K arrivals; folder j folds slices j, j + K, ... (a
-    // slice is one query row x DC columns) once all N have arrived, and the
-    // last folder to finish resets the pair's counters to zero.
-    if (tid == 0) {
-      pend[3] = tk0;
-      pend[7] = tk1;
-      pend[8] = npend;
-    }
-    consumer_sync();
-    constexpr int DSPL = D >= 64 ? D / 32 : 1;
-    const int rows = HG * G, slices = rows * DSPL;
-    float* red = reinterpret_cast<float*>(stages);  // the ring is idle now
-    const int np = pend[8];
-    for (int e = 0; e < np; ++e) {
-      const int pair = pend[4 * e], s0 = pend[4 * e + 1], n_arr = pend[4 * e + 2], tk = pend[4 * e + 3];
-      const int nfold = min(n_arr, slices);
-      if (tk < n_arr - nfold) continue;
-      bool arrived = true;
-      if (tid == 0 && !wait_count_bounded(p.counters + pair, n_arr)) {
-        raise_flag(p, PAD_FLAG_WAIT_TIMEOUT);
-        arrived = false;
-      }
-      // one decision for all consumer warps (a barrier-reduced vote)
-      if (!consumer_vote(arrived && !*abort_flag)) return;
-      const int b = pair / ngroups, hg = pair % ngroups;
-      __half* orow = p.out + b * p.out_sb + (int64_t)(hg * rows) * p.out_sh;
-#pragma unroll 1
-      for (int sl = tk - (n_arr - nfold); sl < slices; sl += nfold) {
-        const int y = sl / DSPL, z = sl % DSPL;
-        fold_slice<D>(p, s0, n_arr, rows, y, z, orow + y * p.out_sh + z * (D / DSPL), red);
-      }
-      if (tid == 0 && atomicAdd(p.counters + kFewPairs + pair, 1) == nfold - 1) {
-        p.counters[pair] = 0;
-        p.counters[kFewPairs + pair] = 0;
-      }
     }
   }
   if (warp == 0 && lane == 0) PAD_STAMP(9);
@@ -1109,8 +892,9 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const float* __res
   pdl_wait_primary();
   if (tid == 0) PAD_MSTAMP(1);
   const int c = tid % C4 + blockIdx.z * C4, sg = tid / C4;
-  FoldState st = fold_empty();
-  // Fold partial slots [s0, s0 + ns) into the state. With a guess, the loads
+  float m = -INFINITY, l = 0.f;
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+  // Fold partial slots [s0, s0 + ns) into (m, l, a). With a guess, the loads
   // (pinned in program order, see ld_nc_*) go out with the descriptor load;
   // a wrong guess folds again from the descriptor (one copy of the loop).
   const int4 meta = ld_nc_i4(ws_meta + w);
@@ -1128,7 +912,6 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const float* __res
       for (int u = 0; u < UNR; ++u) {
         const int su = s + u * PG;
         ml[u] = make_float2(-INFINITY, 0.f);
-        o[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (su < ns) {
           const int64_t row = (int64_t)(s0 + su) * rows + y;
           ml[u] = ld_nc_f2(ws_ml + row);
@@ -1136,32 +919,78 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const float* __res
         }
       }
 #pragma unroll
-      for (int u = 0; u < UNR; ++u) fold_in(st, ml[u], o[u]);
+      for (int u = 0; u < UNR; ++u) {
+        if (ml[u].x == -INFINITY) continue;
+        const float mn = fmaxf(m, ml[u].x);
+        const float al = ex2(m - mn), be = ex2(ml[u].x - mn);
+        l = l * al + ml[u].y * be;
+        a.x = a.x * al + o[u].x * be;
+        a.y = a.y * al + o[u].y * be;
+        a.z = a.z * al + o[u].z * be;
+        a.w = a.w * al + o[u].w * be;
+        m = mn;
+      }
     }
     if (meta.w != 1) return;
     if (meta.y == s0 && meta.z == ns) break;
-    st = fold_empty();
+    m = -INFINITY;
+    l = 0.f;
+    a = make_float4(0.f, 0.f, 0.f, 0.f);
     s0 = meta.y;
     ns = meta.z;
   }
   const int pair = meta.x;
   if (tid == 0) PAD_MSTAMP(3);
-  // Fold the groups of one warp with shuffles, then the warps' states
-  // through shared memory.
-  fold_warp<C4>(st);
+  // Fold the groups of one warp (lanes C4 apart hold the same columns) with
+  // shuffles, then the warps' states through shared memory.
+#pragma unroll
+  for (int o = C4; o < 32; o <<= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), l2 = __shfl_xor_sync(0xffffffffu, l, o);
+    float4 a2;
+    a2.x = __shfl_xor_sync(0xffffffffu, a.x, o);
+    a2.y = __shfl_xor_sync(0xffffffffu, a.y, o);
+    a2.z = __shfl_xor_sync(0xffffffffu, a.z, o);
+    a2.w = __shfl_xor_sync(0xffffffffu, a.w, o);
+    const float mn = fmaxf(m, m2), mu = (mn == -INFINITY) ? 0.f : mn;
+    const float al = ex2(m - mu), be = ex2(m2 - mu);
+    l = l * al + l2 * be;
+    a.x = a.x * al + a2.x * be;
+    a.y = a.y * al + a2.y * be;
+    a.z = a.z * al + a2.z * be;
+    a.w = a.w * al + a2.w * be;
+    m = mn;
+  }
   const int wid = tid >> 5, lid = tid & 31;
   if (lid < C4) {
-    *reinterpret_cast<float4*>(&red_o[wid][lid * 4]) = st.a;
+    *reinterpret_cast<float4*>(&red_o[wid][lid * 4]) = a;
     if (lid == 0) {
-      red_m[wid] = st.m;
-      red_l[wid] = st.l;
+      red_m[wid] = m;
+      red_l[wid] = l;
     }
   }
   __syncthreads();
   if (tid < C4) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int x = 0; x < NW; ++x) M = fmaxf(M, red_m[x]);
+    const float Mu = (M == -INFINITY) ? 0.f : M;
+    float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+    float L = 0.f;
+#pragma unroll
+    for (int x = 0; x < NW; ++x) {
+      const float wt = ex2(red_m[x] - Mu);  // 0 for warps that saw no partial
+      const float4 v = *reinterpret_cast<const float4*>(&red_o[x][tid * 4]);
+      t.x += v.x * wt;
+      t.y += v.y * wt;
+      t.z += v.z * wt;
+      t.w += v.w * wt;
+      L += red_l[x] * wt;
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
     const int b = pair / ngroups, hg = pair % ngroups;
     __half* o = out + b * out_sb + (int64_t)(hg * rows + y) * out_sh + blockIdx.z * DC + tid * 4;
-    fold_write<NW, DC>(red_o, red_m, red_l, tid, o);
+    reinterpret_cast<__half2*>(o)[0] = __floats2half2_rn(t.x * inv, t.y * inv);
+    reinterpret_cast<__half2*>(o)[1] = __floats2half2_rn(t.z * inv, t.w * inv);
     if (tid == 0) PAD_MSTAMP(2);
   }
 }

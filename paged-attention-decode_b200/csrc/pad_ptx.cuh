@@ -148,33 +148,6 @@ __device__ __forceinline__ int4 ld_nc_i4(const int4* p) {
   return v;
 }
 
-// Partials written by other CTAs of the same grid, read after an acquire:
-// through L2 (.cg), never a possibly stale L1 line.
-__device__ __forceinline__ float2 ld_cg_f2(const float2* p) {
-  float2 v;
-  asm volatile("ld.global.cg.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "l"(p));
-  return v;
-}
-__device__ __forceinline__ float4 ld_cg_f4(const float* p) {
-  float4 v;
-  asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
-  return v;
-}
-
-// ---------------------------------------------------------------- GPU-scope sync
-// Arrival on a counter with release semantics: after a CTA barrier, one
-// thread's release covers the whole CTA's earlier global writes.
-__device__ __forceinline__ int atom_add_release_gpu(int* p, int v) {
-  int old;
-  asm volatile("atom.add.release.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
-}
-__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 // ---------------------------------------------------------------- TMA
 // 4-D tiled tensor load global -> shared, completion counted on `bar`.
 __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, uint64_t* bar, int c0, int c1, int c2,

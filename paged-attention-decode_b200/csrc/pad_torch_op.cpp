@@ -77,9 +77,7 @@ void with_workspace(StreamState& st, Launch launch, Need need) {
     size_t bytes = 0;
     check(need(&bytes), "workspace size");
     const int64_t grow = std::max<int64_t>((int64_t)bytes, 2 * st.workspace.numel());
-    // zero-filled once: the library's counters must start at zero, and every
-    // call leaves them zero
-    st.workspace = at::zeros({grow}, st.workspace.options());
+    st.workspace = at::empty({grow}, st.workspace.options());
     rc = launch(st.workspace.data_ptr(), (size_t)st.workspace.numel());
   }
   check(rc, "decode");

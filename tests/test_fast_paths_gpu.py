@@ -6,15 +6,9 @@ parameters are used as loaded; with equal but shorter lengths the cursor has a
 closed form; anything else (ragged lengths, an empty sequence, more than 256
 sequences, a CSR index) takes the scan hand-off. The merge kernel guesses its
 split descriptors for full rows and folds again when the descriptor differs.
-With at most 16 (sequence, KV-head group) pairs the split pairs are merged
-inside the decode kernel instead (arrival counters in the workspace, the last
-CTAs to arrive fold). Each case here lands on one of those paths, with the
-heuristic split count and an explicit one, and is checked against the C oracle.
+Each case here lands on one of those paths, with the heuristic split count and
+an explicit one, and is checked against the C oracle.
 """
-
-import os
-import subprocess
-import sys
 
 import numpy as np
 import pytest
@@ -99,11 +93,12 @@ def _abi_decode(c, ws, num_splits=0):
     return out
 
 
-def test_fused_merge_leaves_counters_zero_across_shapes():
-    """One zero-filled workspace shared by calls of different shapes: fused
-    (few pairs: long context, oversplit with empty partitions, ragged) and
-    unfused (many pairs). Every result matches the oracle and the counter
-    region (the first 256 bytes) is zero after every call."""
+def test_one_workspace_shared_by_calls_of_different_shapes():
+    """One caller-owned workspace (never initialised) reused by calls of
+    different shapes through the C ABI: long context, oversplit with empty
+    partitions, ragged with an empty sequence, many pairs, 8 KV heads with an
+    explicit split count. Every result matches the oracle, whatever the
+    previous call left in the workspace."""
     cases = [
         (explicit_case([20000], num_kv_heads=2, gqa_ratio=6, head_dim=128, page_size=32, seed=51), 0),
         (explicit_case([5], num_kv_heads=2, gqa_ratio=6, head_dim=128, page_size=16, seed=52), 64),
@@ -112,37 +107,9 @@ def test_fused_merge_leaves_counters_zero_across_shapes():
         (explicit_case([2500, 7000], num_kv_heads=8, gqa_ratio=8, head_dim=128, page_size=16, seed=55), 5),
         (explicit_case([20000], num_kv_heads=2, gqa_ratio=6, head_dim=128, page_size=32, seed=51), 0),
     ]
-    ws = torch.zeros(64 << 20, dtype=torch.uint8, device="cuda")
+    ws = torch.full((64 << 20,), 0xA5, dtype=torch.uint8, device="cuda")
     for i, (c, s) in enumerate(cases):
         ref = oracle.decode_c(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens)
         out = _abi_decode(c, ws, s)
         torch.cuda.synchronize()
         assert_parity(out.float().cpu().numpy(), ref, f"case {i} S={s}")
-        assert int(ws[:256].count_nonzero()) == 0, f"case {i}: counters not reset"
-
-
-_UNFUSED_SCRIPT = """
-import sys
-sys.path[:0] = {paths!r}
-import numpy as np, torch, oracle
-from gpu_utils import assert_parity, run
-from pad_b200.cases import config_case, explicit_case
-for c, s in [(config_case("c3", batch=1, seq_len=32768, seed=9), None),
-             (explicit_case([1, 17, 300, 4000], num_kv_heads=2, gqa_ratio=6, head_dim=128, page_size=16, seed=5), 3),
-             (config_case("c2", batch=8), None)]:
-    ref = oracle.decode_c(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens)
-    assert_parity(run(c, num_splits=s), ref, "unfused")
-print("ok")
-"""
-
-
-def test_few_pairs_through_the_merge_kernel_when_fusion_is_off():
-    """PAD_B200_FUSED_MERGE=0 routes few-pair batches through the separate
-    merge kernel (the A/B switch): that path stays correct too."""
-    here = os.path.dirname(os.path.abspath(__file__))
-    root = os.path.dirname(here)
-    paths = [root, os.path.join(root, "paged-attention-decode_b200"), here]
-    env = dict(os.environ, PAD_B200_FUSED_MERGE="0")
-    r = subprocess.run([sys.executable, "-c", _UNFUSED_SCRIPT.format(paths=paths)], env=env, capture_output=True,
-                       text=True, timeout=300)
-    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-3000:]

@@ -90,7 +90,7 @@ def test_noalloc_and_workspace_entries_agree_on_invalid_arguments():
     out = torch.empty_like(q)
     lib = _lib.load()
     stream = torch.cuda.current_stream().cuda_stream
-    ws = torch.zeros(1 << 20, dtype=torch.uint8, device="cuda")  # zero-filled before first use
+    ws = torch.empty(1 << 20, dtype=torch.uint8, device="cuda")
 
     def both(**over):
         a = dict(b=q.shape[0], hq=q.shape[1], hkv=k.shape[2], d=q.shape[2], p=k.shape[0], ps=k.shape[1],
