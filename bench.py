@@ -28,6 +28,8 @@ Extra keys (all printed by this script; the design notes cite them by name):
   host_us_per_call        CPU time of one paged_attention_decode_cuda_v4 call
                           (resident inputs, no copies, no sync inside)
   e2e / e2e_kv_resident   through the public API with host buffers
+  e2e_kv_resident_pipelined  the same with the next step's upload overlapping
+                          this step's decode (two staging buffers, a copy stream)
   cpu_baseline / cpu_port the reference's CPU path (src/reference.py as
                           shipped) / the C restatement, on the host cores
   same_box_*              the reference's Triton v4 and FlashInfer, timed the
@@ -327,6 +329,66 @@ def time_e2e_resident(pool, steps, torch):
     e.record()
     torch.cuda.synchronize()
     return s.elapsed_time(e) / steps, sum(sizes), out_h.numel() * out_h.element_size()
+
+
+def time_e2e_resident_pipelined(pool, steps, torch):
+    """As time_e2e_resident, but the way a serving loop overlaps transfers:
+    two staging buffers, the next step's inputs uploaded on a copy stream
+    while this step decodes, the output copied back on the copy stream once
+    the decode is done. Every step still moves its own inputs H2D and its
+    output D2H; ms per step is the steady-state period."""
+    import pad_b200
+
+    parts = [pool.q.cpu(), pool.block_table.cpu().to(torch.int32), pool.seq_lens.cpu().to(torch.int32)]
+    sizes = [t.numel() * t.element_size() for t in parts]
+    offs = [0]
+    for n in sizes:
+        offs.append(offs[-1] + (n + 255) // 256 * 256)
+    host = torch.empty(offs[-1], dtype=torch.uint8).pin_memory()
+    for t, o, n in zip(parts, offs, sizes):
+        host[o:o + n].copy_(t.contiguous().view(-1).view(torch.uint8))
+    bufs = [torch.empty_like(host, device="cuda") for _ in range(2)]
+    views = [(b[offs[0]:offs[0] + sizes[0]].view(torch.float16).view(pool.q.shape),
+              b[offs[1]:offs[1] + sizes[1]].view(torch.int32).view(pool.block_table.shape),
+              b[offs[2]:offs[2] + sizes[2]].view(torch.int32)) for b in bufs]
+    outs = [torch.empty_like(pool.q) for _ in range(2)]
+    out_h = [torch.empty(pool.q.shape, dtype=torch.float16).pin_memory() for _ in range(2)]
+    comp, copy = torch.cuda.current_stream(), torch.cuda.Stream()
+    up = [torch.cuda.Event() for _ in range(2)]
+    done = [torch.cuda.Event() for _ in range(2)]
+    back = [torch.cuda.Event() for _ in range(2)]
+
+    def run(n):
+        with torch.cuda.stream(copy):
+            bufs[0].copy_(host, non_blocking=True)
+            up[0].record(copy)
+        for i in range(n):
+            cur, nxt = i % 2, (i + 1) % 2
+            if i + 1 < n:
+                with torch.cuda.stream(copy):
+                    copy.wait_event(done[nxt]) if i >= 1 else None  # buffer nxt's last decode finished
+                    bufs[nxt].copy_(host, non_blocking=True)
+                    up[nxt].record(copy)
+            comp.wait_event(up[cur])
+            if i >= 2:
+                comp.wait_event(back[cur])  # outs[cur] copied out two steps ago
+            q, bt, sl = views[cur]
+            pad_b200.paged_attention_decode_cuda_v4(q, pool.k_cache, pool.v_cache, bt, sl, out=outs[cur])
+            done[cur].record(comp)
+            with torch.cuda.stream(copy):
+                copy.wait_event(done[cur])
+                out_h[cur].copy_(outs[cur], non_blocking=True)
+                back[cur].record(copy)
+        comp.wait_stream(copy)
+
+    run(6)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(comp)
+    run(steps)
+    e.record(comp)
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / steps, sum(sizes), out_h[0].numel() * out_h[0].element_size()
 
 
 def host_us_per_call(pool, torch, calls=200):
@@ -631,6 +693,10 @@ def run_ours(args):
             extra["e2e_kv_resident"] = {"value": per_step_bytes / (res_ms * 1e-3) / 1e12, "unit": "TB/s",
                                         "h2d_bytes_per_step": rh2d, "d2h_bytes_per_step": rd2h,
                                         "us_per_call": res_ms * 1e3}
+            pp_ms, ph2d, pd2h = time_e2e_resident_pipelined(pools[0], 200, torch)
+            extra["e2e_kv_resident_pipelined"] = {"value": per_step_bytes / (pp_ms * 1e-3) / 1e12, "unit": "TB/s",
+                                                  "h2d_bytes_per_step": ph2d, "d2h_bytes_per_step": pd2h,
+                                                  "us_per_call": pp_ms * 1e3}
             extra["host_us_per_call"] = host_us_per_call(pools[0], torch)
         del pools
         torch.cuda.empty_cache()
