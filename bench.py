@@ -22,9 +22,12 @@ Extra keys (all printed by this script; the design notes cite them by name):
                           of the reference sweeps the same way)
   c4_llama8b_b256         C4, the ragged Llama-3-8B batch of 256
   c5_strong               C5 (1024 Llama-3-70B sequences) split over the N
-                          ranks through pad_b200.sharded.ShardedDecoder: strong
+                          ranks (equal sequence counts, as the config states)
+                          through pad_b200.sharded.ShardedDecoder: strong
                           scaling, max-rank device time, gather time, sampled
                           oracle check
+  c5_strong_token_balanced  the same with contiguous ranges of near-equal KV
+                          tokens (balanced_ranges), N > 1 only
   host_us_per_call        CPU time of one paged_attention_decode_cuda_v4 call
                           (resident inputs, no copies, no sync inside)
   e2e / e2e_kv_resident   through the public API with host buffers
@@ -566,7 +569,7 @@ def cpu_baselines(cfg, batch, seq_len, seq_lens):
 
 
 # ------------------------------------------------------------------ C5 strong scaling
-def c5_strong(world, rank, local, torch, barrier, peak_gbs, steps=20):
+def c5_strong(world, rank, local, torch, barrier, peak_gbs, steps=20, balanced=False):
     """C5 (1024 Llama-3-70B sequences) split over the ranks: each rank builds
     only its own sequences' KV pages, in a permuted local pool on its GPU,
     and decodes them through the launcher (ShardedDecoder). Device time is
@@ -577,9 +580,17 @@ def c5_strong(world, rank, local, torch, barrier, peak_gbs, steps=20):
     from pad_b200.cases import config_case, kv_bytes
     from pad_b200.sharded import LocalShard, ShardedDecoder, localize
 
-    cfg, b, _, sl = workload_spec("c5", world, rank)
-    c = config_case(cfg, seq_lens=sl, device="cuda", seed=100 + rank)
-    dec = ShardedDecoder(C5_BATCH, world, rank, torch.device("cuda", local))
+    from pad_b200.cases import config_seq_lens
+    from pad_b200.sharded import balanced_ranges
+
+    ranges = balanced_ranges(config_seq_lens("c5"), world) if balanced else None
+    if balanced:
+        lo, hi = ranges[rank]
+        sl = config_seq_lens("c5")[lo:hi]
+    else:
+        _, _, _, sl = workload_spec("c5", world, rank)
+    c = config_case("c5", seq_lens=sl, device="cuda", seed=100 + rank)
+    dec = ShardedDecoder(C5_BATCH, world, rank, torch.device("cuda", local), ranges=ranges)
     shard = LocalShard(dec.lo, dec.hi, c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens)
     nb = kv_bytes(sl, c.k_cache.shape[2], c.k_cache.shape[3])
     ms = time_device([c], steps, 3, torch, barrier, fn=lambda _c: dec.decode(shard)) / steps
@@ -622,7 +633,13 @@ def c5_strong(world, rank, local, torch, barrier, peak_gbs, steps=20):
     else:
         ms_max = ms_min = ms
         bytes_total = bytes_max = bytes_min = nb
-    return {"n_gpus": world, "sequences": C5_BATCH, "sequences_per_gpu_max": math.ceil(C5_BATCH / world),
+    rows = torch.tensor([dec.hi - dec.lo], device="cuda", dtype=torch.int64)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(rows, op=dist.ReduceOp.MAX)
+    return {"n_gpus": world, "sequences": C5_BATCH, "sequences_per_gpu_max": int(rows.item()),
+            "split": "contiguous, near-equal KV tokens per rank" if balanced else "contiguous, equal sequence counts",
             "steps": steps,
             "us_per_call_max_rank": round(ms_max * 1e3, 2), "us_per_call_min_rank": round(ms_min * 1e3, 2),
             "TB_s_aggregate": round(bytes_total / (ms_max * 1e-3) / 1e12, 4),
@@ -702,6 +719,9 @@ def run_ours(args):
         torch.cuda.empty_cache()
         extra["c5_strong"] = c5_strong(world, rank, local, torch, barrier, peak_gbs)
         torch.cuda.empty_cache()
+        if world > 1:
+            extra["c5_strong_token_balanced"] = c5_strong(world, rank, local, torch, barrier, peak_gbs, balanced=True)
+            torch.cuda.empty_cache()
         if rank == 0 and world == 1:
             extra.update(cpu_baselines(cfg, batch, seq_len, seq_lens))
     if not args.no_sweep and world == 1 and args.workload == "c2":

@@ -11,7 +11,9 @@ decode path needs to scale out, written against ``torch.distributed`` so that
 the same logic runs on NCCL over NVLink and, for tests, on gloo over CPU
 processes:
 
-* ``shard_range``     -- which sequences a rank owns;
+* ``shard_range``     -- which sequences a rank owns (equal counts);
+* ``balanced_ranges`` -- contiguous ranges with near-equal KV tokens instead
+                         (ragged batches: the slowest rank sets the step time);
 * ``LocalShard``      -- a rank's own problem: its q rows, its local page pool
                          and its block table in local page ids;
 * ``localize``        -- cut a rank's shard out of a global problem (only that
@@ -40,6 +42,30 @@ def shard_range(batch: int, world: int, rank: int) -> tuple[int, int]:
     return lo, lo + base + (1 if rank < extra else 0)
 
 
+def balanced_ranges(seq_lens, world: int) -> list[tuple[int, int]]:
+    """Contiguous [lo, hi) sequence ranges, one per rank, cut where the running
+    token count crosses k * total / world: each rank's KV bytes are within
+    one sequence of the mean (equal-count ranges can differ by the spread of
+    the lengths). Every rank gets at least one sequence while there are
+    enough; empty ranges only when batch < world."""
+    sl = np.clip(np.asarray(seq_lens, dtype=np.int64), 0, None)
+    batch = len(sl)
+    cum = np.concatenate([[0], np.cumsum(sl)])
+    total = int(cum[-1])
+    cuts = [0]
+    for k in range(1, world):
+        target = total * k / world
+        c = int(np.searchsorted(cum, target, side="left"))
+        # the closer of the two boundaries around the target, kept monotone
+        if c > 0 and abs(cum[c - 1] - target) <= abs(cum[min(c, batch)] - target):
+            c -= 1
+        lo_bound = cuts[-1] + (1 if batch - cuts[-1] >= world - k + 1 else 0)
+        hi_bound = batch - (world - k) if batch >= world else batch
+        cuts.append(int(min(max(c, lo_bound), max(hi_bound, lo_bound))))
+    cuts.append(batch)
+    return [(cuts[r], cuts[r + 1]) for r in range(world)]
+
+
 @dataclass
 class LocalShard:
     """One rank's decode problem: sequences [lo, hi) of the global batch,
@@ -60,7 +86,7 @@ def _as_tensor(a):
 
 
 def localize(q, k_cache, v_cache, block_table, seq_lens, world: int, rank: int, device=None,
-             shuffle_seed: int | None = None) -> LocalShard:
+             shuffle_seed: int | None = None, ranges: list[tuple[int, int]] | None = None) -> LocalShard:
     """Cut rank `rank`'s sequences out of a global problem.
 
     The distinct pages its sequences reference (block_table[b, :ceil(seq_b /
@@ -70,10 +96,11 @@ def localize(q, k_cache, v_cache, block_table, seq_lens, world: int, rank: int, 
     layout like the global one -- and the block table is rewritten to local
     page ids by one ``torch.unique(..., return_inverse=True)``. Unused
     trailing block-table entries become 0. Only the shard moves to ``device``.
-    Works for numpy or torch inputs.
+    ``ranges`` (one [lo, hi) per rank, e.g. from ``balanced_ranges``) replaces
+    the equal-count split. Works for numpy or torch inputs.
     """
     q, k_cache, v_cache, block_table, seq_lens = map(_as_tensor, (q, k_cache, v_cache, block_table, seq_lens))
-    lo, hi = shard_range(q.shape[0], world, rank)
+    lo, hi = ranges[rank] if ranges is not None else shard_range(q.shape[0], world, rank)
     page_size = k_cache.shape[1]
     src = k_cache.device
     sl = seq_lens[lo:hi].to(device=src, dtype=torch.int64).clamp(min=0)
@@ -104,15 +131,17 @@ def localize(q, k_cache, v_cache, block_table, seq_lens, world: int, rank: int, 
                       seq_lens[lo:hi].to(torch.int32).to(dev), page_map.cpu())
 
 
-def gather_to_rank0(out_local: torch.Tensor, batch: int, world: int, group=None):
+def gather_to_rank0(out_local: torch.Tensor, batch: int, world: int, group=None,
+                    ranges: list[tuple[int, int]] | None = None):
     """Gather every rank's output rows to rank 0 in sequence order.
 
-    Shards may differ in size by one sequence, so each rank pads to the
-    largest shard; rank 0 returns the [batch, Hq, D] tensor, others None."""
+    Shards may differ in size, so each rank pads to the largest shard; rank 0
+    returns the [batch, Hq, D] tensor, others None. ``ranges`` as for
+    ``localize`` (default: the equal-count split)."""
     import torch.distributed as dist
 
     rank = dist.get_rank(group)
-    sizes = [shard_range(batch, world, r) for r in range(world)]
+    sizes = ranges if ranges is not None else [shard_range(batch, world, r) for r in range(world)]
     rows = max(h - l for l, h in sizes)
     if out_local.shape[0] == rows:
         pad = out_local.contiguous()
@@ -135,11 +164,13 @@ class ShardedDecoder:
     buffer. ``gather()`` collects the last outputs on rank 0 in global
     sequence order (one NCCL gather; call it only when rank 0 needs them)."""
 
-    def __init__(self, batch_total: int, world: int, rank: int, device, group=None):
+    def __init__(self, batch_total: int, world: int, rank: int, device, group=None,
+                 ranges: list[tuple[int, int]] | None = None):
         self.batch_total, self.world, self.rank = batch_total, world, rank
         self.device = torch.device(device)
         self.group = group
-        self.lo, self.hi = shard_range(batch_total, world, rank)
+        self.ranges = ranges
+        self.lo, self.hi = ranges[rank] if ranges is not None else shard_range(batch_total, world, rank)
         self._out: torch.Tensor | None = None
 
     def decode(self, shard: LocalShard, num_splits=None, scale=None) -> torch.Tensor:
@@ -155,17 +186,20 @@ class ShardedDecoder:
 
     def gather(self, out_local: torch.Tensor | None = None):
         out = self._out if out_local is None else out_local
-        return gather_to_rank0(out, self.batch_total, self.world, self.group)
+        return gather_to_rank0(out, self.batch_total, self.world, self.group, self.ranges)
 
 
 def decode_sharded(q, k_cache, v_cache, block_table, seq_lens, *, world: int, rank: int, device,
-                   num_splits=None, scale=None, gather: bool = True, shuffle_seed: int | None = None):
+                   num_splits=None, scale=None, gather: bool = True, shuffle_seed: int | None = None,
+                   balance_tokens: bool = False):
     """Localize this rank's shard of a global problem (only its pages go to
     `device`), decode it and (optionally) gather the outputs to rank 0.
+    ``balance_tokens`` splits by KV tokens instead of sequence counts.
     Returns (local output, gathered or None)."""
+    ranges = balanced_ranges(_as_tensor(seq_lens).cpu().numpy(), world) if balance_tokens else None
     shard = localize(q, k_cache, v_cache, block_table, seq_lens, world, rank, device=device,
-                     shuffle_seed=shuffle_seed)
-    dec = ShardedDecoder(q.shape[0], world, rank, device)
+                     shuffle_seed=shuffle_seed, ranges=ranges)
+    dec = ShardedDecoder(q.shape[0], world, rank, device, ranges=ranges)
     out = dec.decode(shard, num_splits=num_splits, scale=scale)
     full = dec.gather(out) if gather else None
     return out, full

@@ -107,3 +107,48 @@ def test_sharded_decoder_rejects_another_ranks_shard():
     sh = localize(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens, 2, 1)
     with pytest.raises(ValueError, match="owns sequences"):
         ShardedDecoder(3, 2, 0, "cpu").decode(sh)
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_balanced_ranges_cover_contiguously_with_near_equal_tokens(world):
+    from pad_b200.cases import config_seq_lens
+    from pad_b200.sharded import balanced_ranges
+
+    for sl in (config_seq_lens("c5"), config_seq_lens("c4"), np.array([5, 0, 0, 100, 7, 7000, 3]),
+               np.zeros(9, dtype=np.int64), np.array([3, 1])):
+        r = balanced_ranges(sl, world)
+        assert len(r) == world and r[0][0] == 0 and r[-1][1] == len(sl)
+        assert all(a[1] == b[0] and a[0] <= a[1] for a, b in zip(r, r[1:]))
+        if len(sl) >= world:
+            assert all(h > l for l, h in r)  # every rank gets a sequence when there are enough
+        tok = [int(np.asarray(sl)[l:h].sum()) for l, h in r]
+        # each rank within one (longest) sequence of the mean
+        assert max(tok) - sum(tok) / world <= int(np.max(sl)) + 1 if len(sl) else True
+
+
+def _worker_ranges(rank, world, port, q):
+    from pad_b200.sharded import ShardedDecoder, balanced_ranges
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        c = explicit_case([40, 0, 333, 17, 128, 600, 5, 2000], num_kv_heads=2, gqa_ratio=4, head_dim=32,
+                          page_size=8, seed=4)
+        ranges = balanced_ranges(c.seq_lens, world)
+        sh = localize(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens, world, rank, ranges=ranges)
+        assert (sh.lo, sh.hi) == ranges[rank]
+        out = torch.from_numpy(oracle.decode_c(sh.q.numpy(), sh.k_cache.numpy(), sh.v_cache.numpy(),
+                                               sh.block_table.numpy(), sh.seq_lens.numpy()))
+        full = ShardedDecoder(c.q.shape[0], world, rank, "cpu", ranges=ranges).gather(out)
+        if rank == 0:
+            ref = oracle.decode_c(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens)
+            q.put(float(np.abs(full.numpy() - ref).max()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_gather_with_token_balanced_ranges():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    mp.start_processes(_worker_ranges, args=(3, _free_port(), q), nprocs=3, join=True, start_method="spawn")
+    assert q.get(timeout=60) == 0.0
