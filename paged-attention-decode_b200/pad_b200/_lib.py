@@ -68,7 +68,7 @@ def load() -> ctypes.CDLL:
     global _lib
     if _lib is None:
         if not os.path.exists(LIB_PATH):
-            raise ImportError(f"{LIB_PATH} is missing: build it with `python -m pad_b200.build` "
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python paged-attention-decode_b200/pad_b200/build.py` "
                               "(there is no non-CUDA fallback)")
         lib = ctypes.CDLL(LIB_PATH)
         for name, (res, args) in SIGNATURES.items():
@@ -87,7 +87,7 @@ def ops():
     if _ops is None:
         load()
         if not os.path.exists(OPS_PATH):
-            raise ImportError(f"{OPS_PATH} is missing: build it with `python -m pad_b200.build`")
+            raise ImportError(f"{OPS_PATH} is missing: build it with `python paged-attention-decode_b200/pad_b200/build.py`")
         import torch
 
         torch.ops.load_library(OPS_PATH)

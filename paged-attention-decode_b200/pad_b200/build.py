@@ -2,7 +2,7 @@
 and _pad_torch_ops.so, the thin torch operator library over it
 (torch.ops.pad_b200.*, csrc/pad_torch_op.cpp, host C++ only).
 
-    python -m pad_b200.build            # from paged-attention-decode_b200/
+    python paged-attention-decode_b200/pad_b200/build.py   # (runs without importing pad_b200)
 
 Both libraries are written next to this file so that they travel with the
 source tree; nothing is installed into site-packages.

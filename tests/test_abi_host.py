@@ -153,3 +153,20 @@ def test_heuristic_partitions():
     assert partition.heuristic_partitions(148, 1, 2, 2, 6, 64, 16) == 32      # capped by tiles (2 x 16)
     assert partition.head_group(8, 4) == 8 and partition.head_group(2, 6) == 2 and partition.head_group(6, 1) == 2
     assert partition.head_group(8, 16) == 4 and partition.head_group(3, 2) == 1
+
+
+def test_build_entry_does_not_import_the_package(tmp_path):
+    """__graft_entry__.build() must run on a fresh checkout, before any library
+    exists: the build step is loaded by file path, never through pad_b200."""
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = ("import importlib.util, os, sys; p = os.path.join(%r, 'paged-attention-decode_b200', 'pad_b200', 'build.py');"
+            "s = importlib.util.spec_from_file_location('b', p); m = importlib.util.module_from_spec(s);"
+            "s.loader.exec_module(m); assert 'pad_b200' not in sys.modules; print(m.LIB_PATH)") % root
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr[-2000:]
+    import __graft_entry__
+
+    assert "spec_from_file_location" in open(__graft_entry__.__file__).read()
