@@ -7,6 +7,8 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
+#include <map>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -151,6 +153,19 @@ int prepare_device(int device, const Instance& in, int key, int* num_sms, int* o
   *num_sms = dc.num_sms;
   *occ = dc.occ[key];
   return PAD_OK;
+}
+
+// Integer tuning knob from the environment, read once per name.
+int env_int(const char* name, int dflt) {
+  static std::mutex mu;
+  static std::map<std::string, int> seen;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = seen.find(name);
+  if (it != seen.end()) return it->second;
+  const char* v = std::getenv(name);
+  const int x = v != nullptr ? std::atoi(v) : dflt;
+  seen[name] = x;
+  return x;
 }
 
 // ----------------------------------------------------------------- planning
@@ -467,6 +482,9 @@ int decode_impl(const void* q, const void* k_cache, const void* v_cache, const i
   prm.box_rows_log2 = __builtin_ctz((unsigned)plan.box_rows);
   prm.page_shift = (page_size & (page_size - 1)) == 0 ? __builtin_ctz((unsigned)page_size) : -1;
   prm.meta_by_pair = batch * (num_kv_heads / in.hg) < plan.partitions ? 1 : 0;
+  // guessed first tiles per CTA warmed into L2 before the dependency wait
+  // (PAD_B200_L2_WARM overrides, for A/B timing; 0 turns it off)
+  prm.l2_warm = env_int("PAD_B200_L2_WARM", 4);
   prm.scale_log2 = scale * kLog2e;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);

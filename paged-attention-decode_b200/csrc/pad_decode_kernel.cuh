@@ -63,6 +63,7 @@ struct __align__(64) DecodeParams {
   int box_rows_log2; // log2(R)
   int page_shift;    // log2(page_size) when it is a power of two, else -1
   int meta_by_pair;  // merge descriptors indexed by pair (else by partition)
+  int l2_warm;       // guessed first tiles prefetched into L2 before the dependency wait (0: none)
   float scale_log2;  // scale * log2(e)
 };
 

@@ -224,6 +224,53 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
     }
   }
 
+  // Warm L2 with the first l2_warm guessed tiles while the previous kernel
+  // runs -- the last consumer warp does it, so the producer's path to its
+  // first TMA never waits on it, and the consumers wait for tile 0 anyway:
+  // K/V boxes at the page ids read now (possibly stale -- they only steer
+  // prefetches; the loads after the wait read the ids again), the query rows,
+  // and the seq_lens lines. Reads go through L2 only, so no L1 line can feed
+  // a later non-coherent load a stale value.
+  if (warp == kConsumerWarps - 1 && tg_total > 0 && p.l2_warm > 0) {
+    Cursor pc = uniform_cursor<TR>(tg0, cap, ngroups, p.bt_stride);
+    for (int b = 32 * lane; b < p.batch; b += 32 * 32) prefetch_l2(p.seq_lens + b);
+    int pg[S][TR::NB_PER_LANE];
+    {
+      Cursor lc = pc;
+#pragma unroll
+      for (int k = 0; k < S; ++k) {
+        const int32_t* a[TR::NB_PER_LANE];
+        page_id_ptrs<TR>(p, lc, lane, a);
+#pragma unroll
+        for (int u = 0; u < TR::NB_PER_LANE; ++u)
+          pg[k][u] = (k < p.l2_warm && tg0 + k < tg1 && a[u] != nullptr) ? ld_cg_i32(a[u]) : -1;
+        if (tg0 + k < tg1) cursor_next<TR>(lc, p, cap, ngroups, sseq, cap);
+      }
+    }
+    const uint64_t pol = l2_evict_normal_policy();
+    const int R = p.box_rows;
+#pragma unroll
+    for (int k = 0; k < S; ++k) {
+      if (k < p.l2_warm && tg0 + k < tg1) {
+#pragma unroll
+        for (int u = 0; u < TR::NB_PER_LANE; ++u) {
+          const int page = pg[k][u];
+          if ((unsigned)page >= (unsigned)p.num_pages) continue;
+          const int row = row_in_page(p, pc.i * TT + (lane + 32 * u) * R);
+#pragma unroll
+          for (int sg = 0; sg < TR::NSEG; ++sg) {
+            tma_prefetch_l2_4d(&p.tm_k, sg * (TR::SEGW / 2), row, pc.hg * HG, page, pol);
+            tma_prefetch_l2_4d(&p.tm_v, sg * (TR::SEGW / 2), row, pc.hg * HG, page, pol);
+          }
+        }
+        if (lane == 0 && (k == 0 || pc.i == 0))
+#pragma unroll
+          for (int sg = 0; sg < TR::NSEG; ++sg) tma_prefetch_l2_3d(&p.tm_q, sg * (TR::SEGW / 2), pc.hg * HG * G, pc.b);
+        cursor_next<TR>(pc, p, cap, ngroups, sseq, cap);
+      }
+    }
+  }
+
   // Launched as a programmatic dependent of the previous kernel in the
   // stream: everything above touches only this CTA's shared memory; wait for
   // the previous kernel's results (and for it to finish with the workspace)
