@@ -230,8 +230,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stream_kernel(const __grid
   // K/V boxes at the page ids read now (possibly stale -- they only steer
   // prefetches; the loads after the wait read the ids again), the query rows,
   // and the seq_lens lines. Reads go through L2 only, so no L1 line can feed
-  // a later non-coherent load a stale value.
-  if (warp == kConsumerWarps - 1 && tg_total > 0 && p.l2_warm > 0) {
+  // a later non-coherent load a stale value. Only for CTAs with at least 3
+  // tiles: with 1-2 the warming warp is late for its own short run (measured
+  // +0.4-0.7 us at C2 batch 2 and 4).
+  if (warp == kConsumerWarps - 1 && tg_total > 0 && p.l2_warm > 0 && tg1 - tg0 >= 3) {
     Cursor pc = uniform_cursor<TR>(tg0, cap, ngroups, p.bt_stride);
     for (int b = 32 * lane; b < p.batch; b += 32 * 32) prefetch_l2(p.seq_lens + b);
     int pg[S][TR::NB_PER_LANE];
