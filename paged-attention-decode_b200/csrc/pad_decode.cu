@@ -35,15 +35,21 @@ struct Instance {
   int tt;                      // tokens per tile
 };
 
+// Columns of D one wide-merge CTA folds (the merge grid splits D by it).
+#ifndef PAD_MERGE_COLS
+#define PAD_MERGE_COLS 32
+#endif
+constexpr int kMergeCols = PAD_MERGE_COLS;
+
 template <int D, int NT, int HG, bool SWZ>
 Instance make_instance() {
   using TR = Traits<D, NT, HG, SWZ>;
   Instance in;
   in.kernel = reinterpret_cast<const void*>(&decode_stream_kernel<TR>);
   in.merge_small = reinterpret_cast<const void*>(&merge_kernel<D, 128, 1, 4>);
-  in.merge_mid = reinterpret_cast<const void*>(&merge_kernel<D, 256, (D >= 64 ? D / 32 : 1), 4>);
-  in.merge_large = reinterpret_cast<const void*>(&merge_kernel<D, 256, (D >= 64 ? D / 32 : 1), 8>);
-  in.merge_dsplit = D >= 64 ? D / 32 : 1;
+  in.merge_mid = reinterpret_cast<const void*>(&merge_kernel<D, 256, (D >= 2 * kMergeCols ? D / kMergeCols : 1), 4>);
+  in.merge_large = reinterpret_cast<const void*>(&merge_kernel<D, 256, (D >= 2 * kMergeCols ? D / kMergeCols : 1), 8>);
+  in.merge_dsplit = D >= 2 * kMergeCols ? D / kMergeCols : 1;
   in.smem_bytes = TR::SMEM_BYTES;
   in.segw = TR::SEGW;
   in.swz = SWZ;
