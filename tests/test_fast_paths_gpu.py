@@ -113,3 +113,22 @@ def test_one_workspace_shared_by_calls_of_different_shapes():
         out = _abi_decode(c, ws, s)
         torch.cuda.synchronize()
         assert_parity(out.float().cpu().numpy(), ref, f"case {i} S={s}")
+
+
+def test_block_table_rewritten_in_place_between_calls():
+    """The kernel warms L2 from page ids it reads before its dependency wait
+    (they may be stale); only prefetches follow from them. Rewriting the block
+    table and the KV pages in place between consecutive calls on the same
+    buffers must still give each call's own exact result."""
+    a = explicit_case([2048] * 8, num_kv_heads=2, gqa_ratio=6, head_dim=128, page_size=16, seed=61)
+    b = explicit_case([2048] * 8, num_kv_heads=2, gqa_ratio=6, head_dim=128, page_size=16, seed=62)
+    assert a.k_cache.shape == b.k_cache.shape and a.block_table.shape == b.block_table.shape
+    ga, gb = to_gpu(a), to_gpu(b)
+    q, k, v, bt, sl = (t.clone() for t in ga)
+    out = torch.empty_like(q)
+    for c, g in ((a, ga), (b, gb), (a, ga), (b, gb)):
+        for dst, src in zip((q, k, v, bt, sl), g):
+            dst.copy_(src)
+        paged_attention_decode_cuda_v4(q, k, v, bt, sl, out=out)
+        ref = oracle.decode_c(c.q, c.k_cache, c.v_cache, c.block_table, c.seq_lens)
+        assert_parity(out.float().cpu().numpy(), ref, "rewritten in place")
